@@ -1,0 +1,187 @@
+/*
+ * m3_siso.h -- C ABI of the B200 Mamba-3 SISO scan library (libm3siso.so).
+ *
+ * Plain pointers and sizes only: no CUDA or torch types cross this boundary.  Every
+ * tensor pointer is a DEVICE pointer; `stream` is a cudaStream_t passed as void*
+ * (NULL = legacy default stream).  Calls are stream-ordered and never synchronise the
+ * host.  Each entry point returns M3_OK (0) or a negative M3_ERR_* code, and on error
+ * m3_last_error() returns a thread-local message -- the counterpart of the reference's
+ * Python ValueErrors (mamba3_pallas/kernel_fwd.py:249-277, layout.py:232-235,
+ * layout.py:500-506, reference.py:354-355).
+ *
+ * Layouts follow the reference kernel boundary (mamba3_pallas/kernel_fwd.py:226-248):
+ *   q, k          (B, L, N)      head-shared post-RMSNorm C and B, half-split rotary layout
+ *   v, z, y, dy   (B, H, L, P)
+ *   adt/gamma/scale (B, H, L) f32;  phi (B, H, L, Nr) f32          [preprocessed boundary]
+ *   dt_raw/a_raw/trap_raw (B, L, H) f32; angles (B, L, Nr) f32    [raw boundary]
+ *   q_bias, k_bias (H, N) f32;  d_skip, dt_bias (H) f32
+ *   state: ssm (B, H, P, N) f32, k (B, H, N) f32 rotated-unscaled, v (B, H, P) f32,
+ *          phi (B, H, Nr) f32                  (reference.py:46-63, SISOState)
+ * Strides are in ELEMENTS; the innermost axis (N, P or Nr) must be contiguous.  A zero
+ * stride selects the contiguous default, so a zero-initialised struct describes dense
+ * tensors.
+ */
+#ifndef M3_SISO_H
+#define M3_SISO_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  M3_OK = 0,
+  M3_ERR_ARG = -1,          /* NULL pointer where one is required, bad flag value      */
+  M3_ERR_SHAPE = -2,        /* inconsistent or non-positive dims, L % chunk != 0       */
+  M3_ERR_UNSUPPORTED = -3,  /* (N, P, Nr, chunk, dtype) combination not compiled       */
+  M3_ERR_WORKSPACE = -4,    /* workspace missing or too small                          */
+  M3_ERR_LAUNCH = -5,       /* CUDA launch / attribute error                           */
+};
+
+enum { M3_DTYPE_F32 = 0, M3_DTYPE_BF16 = 1 };
+
+/* Matmul-operand policy (mamba3_pallas/layout.py:243-291, DtypePolicy):
+ * F32  -- every contraction in true fp32;
+ * BF16 -- operands rounded to bf16 where the reference kernel rounds them, fp32
+ *         accumulation, fp32 state. */
+enum { M3_POLICY_F32 = 0, M3_POLICY_BF16 = 1 };
+
+typedef struct M3Dims {
+  int32_t batch, seqlen, nheads, state_dim, headdim, n_angles, chunk;
+} M3Dims;
+
+/* Strides (elements) of a rank-3/4 tensor's outer axes.  For (B, L, N)-shaped tensors
+ * `h` is ignored; for (B, L, H) raw streams the innermost H stride is `h`. */
+typedef struct M3Strides {
+  int64_t b, h, l;
+} M3Strides;
+
+/* ---------------------------------------------------------------------------------
+ * Forward chunked scan.
+ * Replaces kernel_fwd.siso_forward (mamba3_pallas/kernel_fwd.py:204-388) when
+ * raw == 0, and siso.siso_segment's preprocess + primal (mamba3_pallas/siso.py:154-216,
+ * reference.py:160-199) when raw == 1 (softplus / heavy-tail / sigmoid / trapezoid
+ * shift / cumulative angles fused into the kernel).
+ * ------------------------------------------------------------------------------- */
+typedef struct M3FwdArgs {
+  M3Dims dims;
+  int32_t io_dtype;   /* dtype of q, k, v, z, y (M3_DTYPE_*) */
+  int32_t policy;     /* M3_POLICY_* */
+  int32_t raw;        /* 0: preprocessed boundary, 1: raw boundary */
+  float a_floor;      /* raw boundary: A <= -a_floor */
+
+  const void *q, *k;  M3Strides q_st, k_st;
+  const void *v;      M3Strides v_st;
+  const void *z;      M3Strides z_st;   /* gate, NULL = ungated */
+
+  const float *adt, *gamma, *scale;     /* raw == 0 */
+  const float *phi;
+
+  const float *dt_raw, *a_raw, *trap_raw; M3Strides raw_st;  /* raw == 1 */
+  const float *angles;                    M3Strides ang_st;
+  const float *dt_bias;
+
+  const float *q_bias, *k_bias;
+  const float *d_skip;                  /* NULL = no skip */
+
+  /* Carried state: all of ssm/k/v (and coef for raw == 0) or none. */
+  const float *seed_ssm, *seed_k, *seed_v;
+  const float *seed_coef;               /* raw == 0: dt_0 (1 - lam_0), (B, H) */
+  const float *seed_phi;                /* raw == 1: phi_init (B, H, Nr), may be NULL */
+
+  void *y;            M3Strides y_st;
+  float *final_ssm, *final_k, *final_v;
+  float *final_phi;                     /* raw == 1: phi at the last position; may be NULL */
+
+  float *ybar;                          /* optional (B, H, L, P) f32 pre-gate output   */
+  void *chunk_states;                   /* optional (B, H, L/chunk, P, N) chunk-start states */
+  int32_t chunk_states_dtype;           /* M3_DTYPE_* of chunk_states */
+} M3FwdArgs;
+
+int m3_siso_fwd(const M3FwdArgs *args, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Backward.  Replaces kernel_bwd.siso_backward (mamba3_pallas/kernel_bwd.py:534-669;
+ * kernel 103-355, epilogue 592-651) for raw == 0, and additionally the autodiff of
+ * reference.preprocess for raw == 1.  Chunk states are recomputed, not read from the
+ * forward: `workspace` (m3_siso_bwd_workspace_size bytes, 256-byte aligned) holds them.
+ * All gradient outputs are f32 and are overwritten (not accumulated into).
+ * ------------------------------------------------------------------------------- */
+typedef struct M3BwdArgs {
+  M3Dims dims;
+  int32_t io_dtype, policy, raw;
+  float a_floor;
+
+  const void *q, *k;  M3Strides q_st, k_st;
+  const void *v;      M3Strides v_st;
+  const void *z;      M3Strides z_st;
+  const float *adt, *gamma, *scale, *phi;
+  const float *dt_raw, *a_raw, *trap_raw; M3Strides raw_st;
+  const float *angles;                    M3Strides ang_st;
+  const float *dt_bias;
+  const float *q_bias, *k_bias, *d_skip;
+  const float *seed_ssm, *seed_k, *seed_v, *seed_coef, *seed_phi;
+
+  const void *dy;     M3Strides dy_st;    /* cotangent of the gated output y */
+  const float *dfinal_ssm, *dfinal_k, *dfinal_v, *dfinal_phi;  /* each may be NULL */
+
+  float *dq, *dk;                         /* (B, L, N), summed over heads */
+  float *dv;                              /* (B, H, L, P) */
+  float *dz;                              /* (B, H, L, P); required iff z != NULL */
+  float *dadt, *dgamma, *dscale, *dphi;   /* raw == 0 */
+  float *ddt_raw, *da_raw, *dtrap_raw;    /* raw == 1, (B, L, H) dense */
+  float *dangles;                         /* raw == 1, (B, L, Nr) dense */
+  float *ddt_bias;                        /* raw == 1, (H) */
+  float *dq_bias, *dk_bias;               /* (H, N) */
+  float *dd_skip;                         /* (H); required iff d_skip != NULL */
+  float *dseed_ssm, *dseed_k, *dseed_v;   /* required iff a seed is given */
+  float *dseed_coef;                      /* raw == 0 with a seed */
+  float *dseed_phi;                       /* raw == 1 with seed_phi */
+
+  void *workspace;
+  size_t workspace_bytes;
+} M3BwdArgs;
+
+size_t m3_siso_bwd_workspace_size(const M3Dims *dims);
+int m3_siso_bwd(const M3BwdArgs *args, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Single-token decode step.  Replaces kernel_decode.decode_step / siso_decode /
+ * siso_decode_folded (mamba3_pallas/kernel_decode.py:252-471).  The state buffers are
+ * updated IN PLACE (the reference donates them: kernel_decode.py:350-352, 454).
+ * raw == 1 also fuses lm_decode_step's length-1 preprocess (model.py:274-277).
+ * ------------------------------------------------------------------------------- */
+typedef struct M3DecodeArgs {
+  int32_t batch, nheads, state_dim, headdim, n_angles;
+  int32_t io_dtype, policy, raw;
+  float a_floor;
+  const void *q, *k;          /* (B, N) */
+  int64_t qk_stride_b;        /* 0 = N */
+  const void *v, *z;          /* (B, H, P), z may be NULL */
+  int64_t vz_stride_b;        /* 0 = H * P (head stride is P) */
+  const float *adt, *dt, *lam;            /* raw == 0: (B, H) */
+  const float *dt_raw, *a_raw, *trap_raw; /* raw == 1: (B, H) */
+  int64_t raw_stride_b;                   /* 0 = H */
+  const float *dt_bias;                   /* raw == 1 */
+  const float *angles;        /* (B, Nr) raw pre-tanh rates */
+  int64_t ang_stride_b;       /* 0 = Nr */
+  const float *q_bias, *k_bias, *d_skip;
+  float *ssm, *state_k, *state_v, *phi;   /* in/out */
+  void *y;                    /* (B, H, P) io_dtype */
+} M3DecodeArgs;
+
+int m3_siso_decode(const M3DecodeArgs *args, void *stream);
+
+/* Last error message of this thread ("" if none). */
+const char *m3_last_error(void);
+
+/* Library version, for the bindings' load check. */
+int m3_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3_SISO_H */

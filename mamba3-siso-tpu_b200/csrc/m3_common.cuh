@@ -1,0 +1,72 @@
+// Shared device helpers for the Mamba-3 SISO kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "m3_siso.h"
+
+namespace m3 {
+
+constexpr float kPi = 3.14159265358979323846f;
+constexpr float kTwoPi = 6.28318530717958647692f;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kSimtThreads = 256;  // block size of the generic CUDA-core kernels
+
+template <typename T> __device__ __forceinline__ float ld(const T* p);
+template <> __device__ __forceinline__ float ld<float>(const float* p) { return *p; }
+template <> __device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+template <typename T> __device__ __forceinline__ void stg(T* p, float x);
+template <> __device__ __forceinline__ void stg<float>(float* p, float x) { *p = x; }
+template <> __device__ __forceinline__ void stg<__nv_bfloat16>(__nv_bfloat16* p, float x) {
+  *p = __float2bfloat16_rn(x);
+}
+
+// Round-to-nearest-even through bf16: the matmul-operand cast of the BF16 policy
+// (mamba3_pallas/kernel_fwd.py:139-141).
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+template <bool MMB> __device__ __forceinline__ float mmr(float x) { return MMB ? bf16r(x) : x; }
+
+// softplus(x) = max(x, 0) + log1p(exp(-|x|))  (jax.nn.softplus, reference.py:186)
+__device__ __forceinline__ float softplusf(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + expf(-x)); }
+// heavy_tail(x) = max(x,0) + 1/(1 - min(x,0))  (reference.py:202-209)
+__device__ __forceinline__ float heavy_tail(float x) { return fmaxf(x, 0.f) + 1.f / (1.f - fminf(x, 0.f)); }
+// phi - 2 pi floor(phi / 2 pi)  (reference.py:156)
+__device__ __forceinline__ float wrap2pi(float x) { return x - kTwoPi * floorf(x / kTwoPi); }
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// Inclusive scan over the 32 lanes of a warp.
+__device__ __forceinline__ float warp_inclusive_scan(float x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
+}
+
+// Output-tile geometry for an (M x NC) block computed by NT threads: thread (ty, tx)
+// owns rows ty + RY*i and columns tx + RX*j (strided so neighbouring lanes touch
+// neighbouring shared-memory banks).
+template <int M, int NC, int NT>
+struct Tile {
+  static constexpr int RX = NC < 16 ? NC : 16;
+  static constexpr int RY = NT / RX;
+  static constexpr int TM = M / RY;
+  static constexpr int TN = NC / RX;
+  static_assert(NT % RX == 0, "tile");
+  static_assert(M % RY == 0 && TM >= 1, "tile rows");
+  static_assert(NC % RX == 0, "tile cols");
+};
+
+}  // namespace m3

@@ -1,0 +1,38 @@
+// Host-side internals shared by the translation units of libm3siso.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "m3_siso.h"
+
+namespace m3 {
+
+// Records a thread-local error message and returns `code`.
+int set_error(int code, const std::string& msg);
+// Checks the launch that was just issued.
+int check_launch(const char* what);
+
+// Supported (N, P) pairs of the generic kernels.
+bool supported_np(int n, int p);
+
+int launch_fwd_simt(const M3FwdArgs& a, cudaStream_t s);
+int launch_bwd_simt(const M3BwdArgs& a, cudaStream_t s);
+int launch_decode(const M3DecodeArgs& a, cudaStream_t s);
+size_t bwd_workspace_bytes(const M3Dims& d);
+
+}  // namespace m3
+
+// Instantiate `FN<N, P, T, MMB>` for the supported shapes; `call` is a lambda-like macro
+// argument receiving the instantiated function.  Returns M3_ERR_UNSUPPORTED otherwise.
+#define M3_DISPATCH_NP(n, p, X)                          \
+  do {                                                   \
+    if ((n) == 16 && (p) == 16) { X(16, 16); }           \
+    else if ((n) == 32 && (p) == 16) { X(32, 16); }      \
+    else if ((n) == 32 && (p) == 32) { X(32, 32); }      \
+    else if ((n) == 64 && (p) == 64) { X(64, 64); }      \
+    else if ((n) == 128 && (p) == 64) { X(128, 64); }    \
+    else return m3::set_error(M3_ERR_UNSUPPORTED, "unsupported (state_dim, headdim) = (" + \
+                              std::to_string(n) + ", " + std::to_string(p) + ")"); \
+  } while (0)

@@ -1,0 +1,140 @@
+"""ctypes binding of ``include/m3_siso.h`` (libm3siso.so).
+
+This is the whole host->device boundary: plain structs of pointers and sizes, one call
+per kernel, an int status and a thread-local message.  The library is loaded from this
+package's ``_lib/`` directory; there is no fallback -- if it is missing the import of any
+op fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libm3siso.so")
+
+M3_OK = 0
+M3_ERR_ARG = -1
+M3_ERR_SHAPE = -2
+M3_ERR_UNSUPPORTED = -3
+M3_ERR_WORKSPACE = -4
+M3_ERR_LAUNCH = -5
+M3_DTYPE_F32 = 0
+M3_DTYPE_BF16 = 1
+M3_POLICY_F32 = 0
+M3_POLICY_BF16 = 1
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+
+class M3Dims(ctypes.Structure):
+    _fields_ = [("batch", _i32), ("seqlen", _i32), ("nheads", _i32), ("state_dim", _i32),
+                ("headdim", _i32), ("n_angles", _i32), ("chunk", _i32)]
+
+
+class M3Strides(ctypes.Structure):
+    _fields_ = [("b", _i64), ("h", _i64), ("l", _i64)]
+
+
+class M3FwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("dims", M3Dims), ("io_dtype", _i32), ("policy", _i32), ("raw", _i32), ("a_floor", _f32),
+        ("q", _vp), ("k", _vp), ("q_st", M3Strides), ("k_st", M3Strides),
+        ("v", _vp), ("v_st", M3Strides), ("z", _vp), ("z_st", M3Strides),
+        ("adt", _vp), ("gamma", _vp), ("scale", _vp), ("phi", _vp),
+        ("dt_raw", _vp), ("a_raw", _vp), ("trap_raw", _vp), ("raw_st", M3Strides),
+        ("angles", _vp), ("ang_st", M3Strides), ("dt_bias", _vp),
+        ("q_bias", _vp), ("k_bias", _vp), ("d_skip", _vp),
+        ("seed_ssm", _vp), ("seed_k", _vp), ("seed_v", _vp), ("seed_coef", _vp), ("seed_phi", _vp),
+        ("y", _vp), ("y_st", M3Strides),
+        ("final_ssm", _vp), ("final_k", _vp), ("final_v", _vp), ("final_phi", _vp),
+        ("ybar", _vp), ("chunk_states", _vp), ("chunk_states_dtype", _i32),
+    ]
+
+
+class M3BwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("dims", M3Dims), ("io_dtype", _i32), ("policy", _i32), ("raw", _i32), ("a_floor", _f32),
+        ("q", _vp), ("k", _vp), ("q_st", M3Strides), ("k_st", M3Strides),
+        ("v", _vp), ("v_st", M3Strides), ("z", _vp), ("z_st", M3Strides),
+        ("adt", _vp), ("gamma", _vp), ("scale", _vp), ("phi", _vp),
+        ("dt_raw", _vp), ("a_raw", _vp), ("trap_raw", _vp), ("raw_st", M3Strides),
+        ("angles", _vp), ("ang_st", M3Strides), ("dt_bias", _vp),
+        ("q_bias", _vp), ("k_bias", _vp), ("d_skip", _vp),
+        ("seed_ssm", _vp), ("seed_k", _vp), ("seed_v", _vp), ("seed_coef", _vp), ("seed_phi", _vp),
+        ("dy", _vp), ("dy_st", M3Strides),
+        ("dfinal_ssm", _vp), ("dfinal_k", _vp), ("dfinal_v", _vp), ("dfinal_phi", _vp),
+        ("dq", _vp), ("dk", _vp), ("dv", _vp), ("dz", _vp),
+        ("dadt", _vp), ("dgamma", _vp), ("dscale", _vp), ("dphi", _vp),
+        ("ddt_raw", _vp), ("da_raw", _vp), ("dtrap_raw", _vp), ("dangles", _vp), ("ddt_bias", _vp),
+        ("dq_bias", _vp), ("dk_bias", _vp), ("dd_skip", _vp),
+        ("dseed_ssm", _vp), ("dseed_k", _vp), ("dseed_v", _vp), ("dseed_coef", _vp), ("dseed_phi", _vp),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class M3DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i32), ("nheads", _i32), ("state_dim", _i32), ("headdim", _i32), ("n_angles", _i32),
+        ("io_dtype", _i32), ("policy", _i32), ("raw", _i32), ("a_floor", _f32),
+        ("q", _vp), ("k", _vp), ("qk_stride_b", _i64),
+        ("v", _vp), ("z", _vp), ("vz_stride_b", _i64),
+        ("adt", _vp), ("dt", _vp), ("lam", _vp),
+        ("dt_raw", _vp), ("a_raw", _vp), ("trap_raw", _vp), ("raw_stride_b", _i64),
+        ("dt_bias", _vp), ("angles", _vp), ("ang_stride_b", _i64),
+        ("q_bias", _vp), ("k_bias", _vp), ("d_skip", _vp),
+        ("ssm", _vp), ("state_k", _vp), ("state_v", _vp), ("phi", _vp),
+        ("y", _vp),
+    ]
+
+
+EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
+           "m3_last_error", "m3_version")
+
+_lib = None
+
+
+def lib():
+    """Load libm3siso.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise RuntimeError(
+                f"libm3siso.so not found at {_LIB_PATH}; build it with "
+                "`python mamba3-siso-tpu_b200/build.py` (there is no fallback path)")
+        L = ctypes.CDLL(_LIB_PATH)
+        L.m3_siso_fwd.argtypes = [ctypes.POINTER(M3FwdArgs), _vp]
+        L.m3_siso_fwd.restype = ctypes.c_int
+        L.m3_siso_bwd.argtypes = [ctypes.POINTER(M3BwdArgs), _vp]
+        L.m3_siso_bwd.restype = ctypes.c_int
+        L.m3_siso_bwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]
+        L.m3_siso_bwd_workspace_size.restype = ctypes.c_size_t
+        L.m3_siso_decode.argtypes = [ctypes.POINTER(M3DecodeArgs), _vp]
+        L.m3_siso_decode.restype = ctypes.c_int
+        L.m3_last_error.argtypes = []
+        L.m3_last_error.restype = ctypes.c_char_p
+        L.m3_version.argtypes = []
+        L.m3_version.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def library_path() -> str:
+    return _LIB_PATH
+
+
+class M3Error(ValueError):
+    """A non-zero status from the library (subclasses ValueError like the reference's
+    argument errors)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+def check(rc: int):
+    if rc != M3_OK:
+        raise M3Error(rc, lib().m3_last_error().decode())

@@ -1,0 +1,76 @@
+"""Tensor -> C-ABI plumbing shared by the kernel wrappers."""
+
+from __future__ import annotations
+
+import torch
+
+from . import _capi as C
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the Mamba-3 SISO kernels run on CUDA tensors only (no CPU path)")
+
+
+def io_dtype(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return C.M3_DTYPE_BF16
+    if dt == torch.float32:
+        return C.M3_DTYPE_F32
+    raise ValueError(f"unsupported dtype {dt}; want bfloat16 or float32")
+
+
+def policy_code(name: str) -> int:
+    key = name.strip().lower()
+    if key in ("bf16", "bfloat16", "default"):
+        return C.M3_POLICY_BF16
+    if key in ("f32", "fp32", "float32", "highest"):
+        return C.M3_POLICY_F32
+    raise ValueError(f"Unknown dtype policy {name!r}; want 'bf16' or 'f32'")
+
+
+def f32c(t):
+    """fp32, innermost-contiguous (outer strides are passed through)."""
+    if t is None:
+        return None
+    if t.dtype != torch.float32:
+        t = t.float()
+    if t.dim() and t.stride(-1) != 1:
+        t = t.contiguous()
+    return t
+
+
+def f32dense(t):
+    return None if t is None else t.float().contiguous()
+
+
+def inner_contig(t, dtype):
+    if t is None:
+        return None
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    return t
+
+
+def st_bln(t) -> C.M3Strides:
+    """(B, L, X) with contiguous X."""
+    return C.M3Strides(t.stride(0), 0, t.stride(1))
+
+
+def st_bhlp(t) -> C.M3Strides:
+    return C.M3Strides(t.stride(0), t.stride(1), t.stride(2))
+
+
+def st_blh(t) -> C.M3Strides:
+    return C.M3Strides(t.stride(0), t.stride(2), t.stride(1))

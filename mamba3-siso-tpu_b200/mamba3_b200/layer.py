@@ -1,0 +1,163 @@
+"""The Mamba-3 SISO layer around the scan (``mamba3_pallas/layer.py``).
+
+    in_proj -> [z, x, B, C, dd_dt, dd_A, trap, angles]
+    B, C    -> RMSNorm
+    scan    -> gated by silu(z)        (C is the query, B the key)
+    out_proj
+
+The projections are torch (cuBLAS) GEMMs; every slice of the fused projection reaches
+the scan kernel as a strided view -- no transposes or copies of x, z or the scalar
+streams -- and the kernel writes y straight into the (B, L, H, P) layout out_proj reads.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import itertools
+import math
+from typing import NamedTuple, Optional
+
+import torch
+
+from . import layout as L
+from . import siso as SISO
+from .state import SISOState
+
+
+@dataclasses.dataclass(frozen=True)
+class SISOConfig:
+    """``layer.py:39-99``.  ``chunk`` must be a positive multiple of 64 here (the
+    reference demands a multiple of 128, a TPU lane rule with no B200 counterpart)."""
+
+    d_model: int
+    d_state: int = 128
+    headdim: int = 64
+    expand: int = 2
+    rope_fraction: float = 0.5
+    chunk: int = 128
+    a_floor: float = 1e-4
+    norm_eps: float = 1e-5
+    dt_min: float = 0.001
+    dt_max: float = 0.1
+    dt_init_floor: float = 1e-4
+    policy_name: str = "bf16"
+
+    @property
+    def d_inner(self) -> int:
+        return self.expand * self.d_model
+
+    @property
+    def nheads(self) -> int:
+        if self.d_inner % self.headdim != 0:
+            raise ValueError(f"d_inner {self.d_inner} not divisible by headdim {self.headdim}")
+        return self.d_inner // self.headdim
+
+    @property
+    def n_angles(self) -> int:
+        if self.rope_fraction not in (0.5, 1.0):
+            raise ValueError(f"rope_fraction must be 0.5 or 1.0, got {self.rope_fraction}")
+        width = int(self.d_state * self.rope_fraction)
+        if width % 2:
+            width -= 1
+        n = width // 2
+        if n <= 0:
+            raise ValueError("rope_fraction too small: no rotary angles")
+        return n
+
+    @property
+    def d_in_proj(self) -> int:
+        return 2 * self.d_inner + 2 * self.d_state + 3 * self.nheads + self.n_angles
+
+    def __post_init__(self):
+        L.validate_chunk(self.chunk)
+        L.policy(self.policy_name)
+        _ = self.nheads, self.n_angles
+
+
+class SISOParams(NamedTuple):
+    """``layer.py:102-124``: in_proj ``(d_model, d_in_proj)``, out_proj
+    ``(d_inner, d_model)``, dt_bias ``(H,)``, norm gains ``(N,)``, biases ``(H, N)``
+    (permuted layout), d_skip ``(H,)``."""
+
+    in_proj: torch.Tensor
+    out_proj: torch.Tensor
+    dt_bias: torch.Tensor
+    b_norm_weight: torch.Tensor
+    c_norm_weight: torch.Tensor
+    b_bias: torch.Tensor
+    c_bias: torch.Tensor
+    d_skip: torch.Tensor
+
+
+def _gen(key, device):
+    if isinstance(key, torch.Generator):
+        return key
+    g = torch.Generator(device="cpu")
+    g.manual_seed(int(key))
+    return g
+
+
+def init_params(cfg: SISOConfig, key=0, dtype=torch.float32, device="cuda") -> SISOParams:
+    """``layer.py:127-160``: uniform ``+-1/sqrt(fan_in)`` projections, ``dt_bias`` the
+    inverse softplus of a log-uniform ``[dt_min, dt_max]`` draw, norms / biases / D = 1.
+    ``key`` is an int seed or a CPU ``torch.Generator`` (jax.random streams cannot be
+    reproduced without JAX, so the values -- not the distributions -- differ)."""
+    g = _gen(key, device)
+    s_in = 1.0 / math.sqrt(cfg.d_model)
+    s_out = 1.0 / math.sqrt(cfg.d_inner)
+    u = torch.rand(cfg.nheads, generator=g, dtype=torch.float32)
+    dt = torch.exp(u * (math.log(cfg.dt_max) - math.log(cfg.dt_min)) + math.log(cfg.dt_min))
+    dt = torch.clamp(dt, min=cfg.dt_init_floor)
+    dt_bias = dt + torch.log(-torch.expm1(-dt))
+    in_proj = (torch.rand(cfg.d_model, cfg.d_in_proj, generator=g) * 2 - 1) * s_in
+    out_proj = (torch.rand(cfg.d_inner, cfg.d_model, generator=g) * 2 - 1) * s_out
+    to = dict(dtype=dtype, device=device)
+    return SISOParams(
+        in_proj=in_proj.to(**to), out_proj=out_proj.to(**to), dt_bias=dt_bias.to(**to),
+        b_norm_weight=torch.ones(cfg.d_state, **to), c_norm_weight=torch.ones(cfg.d_state, **to),
+        b_bias=torch.ones(cfg.nheads, cfg.d_state, **to), c_bias=torch.ones(cfg.nheads, cfg.d_state, **to),
+        d_skip=torch.ones(cfg.nheads, **to))
+
+
+def split_in_proj(proj: torch.Tensor, cfg: SISOConfig):
+    """``layer.py:163-187``: ``(z, x, B, C, dt_raw, a_raw, trap_raw, angles)`` as views;
+    z / x come back ``(B, L, H, P)``."""
+    sizes = (cfg.d_inner, cfg.d_inner, cfg.d_state, cfg.d_state, cfg.nheads, cfg.nheads, cfg.nheads, cfg.n_angles)
+    z, x, b, c, dt_raw, a_raw, trap_raw, angles = torch.split(proj, sizes, dim=-1)
+    lead = proj.shape[:-1]
+    return (z.unflatten(-1, (cfg.nheads, cfg.headdim)), x.unflatten(-1, (cfg.nheads, cfg.headdim)),
+            b, c, dt_raw, a_raw, trap_raw, angles)
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """``layer.py:190-198``: f32 internally, gain after scaling, cast back."""
+    xf = x.float()
+    rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * rstd * weight.float()).to(x.dtype)
+
+
+def _scalar_streams(proj: torch.Tensor, cfg: SISOConfig):
+    """The dt / A / trap / angle columns as fp32 strided views (one cast, no transposes)."""
+    start = 2 * cfg.d_inner + 2 * cfg.d_state
+    tail = proj[..., start:]
+    if tail.dtype != torch.float32:
+        tail = tail.float()
+    h = cfg.nheads
+    return tail[..., :h], tail[..., h:2 * h], tail[..., 2 * h:3 * h], tail[..., 3 * h:]
+
+
+def mamba3_siso_layer(params: SISOParams, u: torch.Tensor, cfg: SISOConfig, state: Optional[SISOState] = None):
+    """``layer.py:201-262``: ``u (B, L, d_model)`` -> ``(out (B, L, d_model), SISOState)``."""
+    bsz, seqlen, _ = u.shape
+    proj = torch.matmul(u, params.in_proj.to(u.dtype))
+    z, x, b, c, _, _, _, _ = split_in_proj(proj, cfg)
+    dt_raw, a_raw, trap_raw, angles = _scalar_streams(proj, cfg)
+    b = rms_norm(b, params.b_norm_weight, cfg.norm_eps)
+    c = rms_norm(c, params.c_norm_weight, cfg.norm_eps)
+    out = SISO.siso_segment(
+        q=c, k=b, v=x.permute(0, 2, 1, 3), dt_raw=dt_raw, a_raw=a_raw, trap_raw=trap_raw, angles=angles,
+        dt_bias=params.dt_bias, q_bias=params.c_bias, k_bias=params.b_bias, d_skip=params.d_skip,
+        z=z.permute(0, 2, 1, 3), state=state, a_floor=cfg.a_floor, chunk=cfg.chunk,
+        policy_name=cfg.policy_name, y_blhp=True)
+    y = out.y.permute(0, 2, 1, 3).reshape(bsz, seqlen, cfg.d_inner)
+    return torch.matmul(y.to(u.dtype), params.out_proj.to(u.dtype)), out.state

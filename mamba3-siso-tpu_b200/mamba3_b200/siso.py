@@ -1,0 +1,134 @@
+"""Differentiable boundary (``mamba3_pallas/siso.py``) as torch autograd Functions.
+
+`siso` is the preprocessed-boundary core (``siso.py:39-151``: q, k, v, adt, gamma,
+scale, phi, biases, D, z, seeds -> y and the final state).  `siso_segment` is the entry
+point a layer calls (``siso.py:154-216``); unlike the reference it does not run the
+preprocessing as separate ops: softplus / heavy-tail / sigmoid / the trapezoid shift and
+the cumulative angles are fused into the forward and backward kernels (the raw
+boundary of libm3siso.so).  The forward saves only its inputs; the backward kernel
+recomputes the chunk states.
+"""
+
+from __future__ import annotations
+
+from typing import NamedTuple, Optional
+
+import torch
+
+from . import kernel_bwd as KB
+from . import kernel_fwd as KF
+from .state import SISOState
+
+
+class SISOOutput(NamedTuple):
+    """``siso.py:27-36``."""
+
+    y: torch.Tensor
+    state: SISOState
+
+
+def _need(x):
+    return x is not None and x.requires_grad
+
+
+class _SisoFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip, z, seed_ssm, seed_kv, seed_coef,
+                chunk, policy_name):
+        n = q.shape[-1]
+        sk = seed_kv[..., :n] if seed_kv is not None else None
+        sv = seed_kv[..., n:] if seed_kv is not None else None
+        y, fs, fk, fv = KF.siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=d_skip, z=z,
+                                        seed_ssm=seed_ssm, seed_k=sk, seed_v=sv, seed_coef=seed_coef,
+                                        chunk=chunk, dtype_policy=policy_name)
+        ctx.save_for_backward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip, z, seed_ssm, seed_kv, seed_coef)
+        ctx.meta = (chunk, policy_name)
+        return y, fs, fk, fv
+
+    @staticmethod
+    def backward(ctx, dy, dfs, dfk, dfv):
+        q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip, z, seed_ssm, seed_kv, seed_coef = ctx.saved_tensors
+        chunk, policy_name = ctx.meta
+        n = q.shape[-1]
+        sk = seed_kv[..., :n] if seed_kv is not None else None
+        sv = seed_kv[..., n:] if seed_kv is not None else None
+        if dy is None:
+            dy = torch.zeros_like(v)
+        g = KB.siso_backward(dy, q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=d_skip, z=z,
+                             seed_ssm=seed_ssm, seed_k=sk, seed_v=sv, seed_coef=seed_coef,
+                             dfinal_ssm=dfs, dfinal_k=dfk, dfinal_v=dfv, chunk=chunk, dtype_policy=policy_name)
+        dseed_kv = torch.cat([g.dseed_k, g.dseed_v], dim=-1) if seed_kv is not None else None
+
+        def like(x, p):
+            return None if (p is None or x is None) else x.to(p.dtype)
+
+        return (like(g.dq, q), like(g.dk, k), like(g.dv, v), like(g.dadt, adt), like(g.dgamma, gamma),
+                like(g.dscale, scale), like(g.dphi, phi), like(g.dq_bias, q_bias), like(g.dk_bias, k_bias),
+                like(g.dd_skip, d_skip), like(g.dz, z), like(g.dseed_ssm, seed_ssm), like(dseed_kv, seed_kv),
+                like(g.dseed_coef, seed_coef), None, None)
+
+
+def siso(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip, z, seed_ssm, seed_kv, seed_coef,
+         chunk: int = 128, policy_name: str = "bf16"):
+    """``siso.py:39-91``: returns ``(y, final_ssm, final_k, final_v)``."""
+    return _SisoFn.apply(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip, z, seed_ssm, seed_kv,
+                         seed_coef, chunk, policy_name)
+
+
+class _SegmentFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip,
+                seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, policy_name, y_blhp):
+        y_out = None
+        if y_blhp:  # write y straight into a (B, L, H, P) buffer, seen as (B, H, L, P)
+            b_, l_, h_, p_ = v.shape[0], v.shape[2], v.shape[1], v.shape[3]
+            y_out = torch.empty(b_, l_, h_, p_, dtype=v.dtype, device=v.device).permute(0, 2, 1, 3)
+        y, fs, fk, fv, fphi = KF.siso_forward_raw(
+            q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
+            seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, a_floor=a_floor,
+            chunk=chunk, dtype_policy=policy_name, y_out=y_out)
+        ctx.save_for_backward(q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip,
+                              seed_ssm, seed_k, seed_v, seed_phi)
+        ctx.meta = (a_floor, chunk, policy_name)
+        return y, fs, fk, fv, fphi
+
+    @staticmethod
+    def backward(ctx, dy, dfs, dfk, dfv, dfphi):
+        (q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip,
+         seed_ssm, seed_k, seed_v, seed_phi) = ctx.saved_tensors
+        a_floor, chunk, policy_name = ctx.meta
+        if dy is None:
+            dy = torch.zeros(v.shape, dtype=v.dtype, device=v.device)
+        g = KB.siso_backward_raw(
+            dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
+            seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, dfinal_ssm=dfs,
+            dfinal_k=dfk, dfinal_v=dfv, dfinal_phi=dfphi, a_floor=a_floor, chunk=chunk,
+            dtype_policy=policy_name)
+
+        def like(x, p):
+            return None if (p is None or x is None) else x.to(p.dtype)
+
+        return (like(g.dq, q), like(g.dk, k), like(g.dv, v), like(g.dz, z), like(g.ddt_raw, dt_raw),
+                like(g.da_raw, a_raw), like(g.dtrap_raw, trap_raw), like(g.dangles, angles),
+                like(g.ddt_bias, dt_bias), like(g.dq_bias, q_bias), like(g.dk_bias, k_bias),
+                like(g.dd_skip, d_skip), like(g.dseed_ssm, seed_ssm), like(g.dseed_k, seed_k),
+                like(g.dseed_v, seed_v), like(g.dseed_phi, seed_phi), None, None, None, None)
+
+
+def siso_segment(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=None, z=None,
+                 state: Optional[SISOState] = None, a_floor: float = 1e-4, chunk: int = 128,
+                 policy_name: str = "bf16", y_blhp: bool = False) -> SISOOutput:
+    """``siso.py:154-216``: raw in_proj slices in, ``SISOOutput(y, SISOState)`` out.
+
+    A carried ``state`` seeds the scan with ``dt_0 (1 - lam_0) v_prev k_prev^T`` and its
+    ``phi`` continues the cumulative angles, computed from this segment's own inputs --
+    the segmentation rule of ``siso.py:176-181``.  Differentiable in every tensor input,
+    the carried state included.  ``y_blhp`` makes ``y`` a ``(B, H, L, P)`` view of a
+    ``(B, L, H, P)`` buffer, which is what the layer's out_proj wants.
+    """
+    sp = sk = sv = sphi = None
+    if state is not None:
+        sp, sk, sv, sphi = state.ssm, state.k, state.v, state.phi
+    y, fs, fk, fv, fphi = _SegmentFn.apply(q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias,
+                                           d_skip, sp, sk, sv, sphi, a_floor, chunk, policy_name, y_blhp)
+    return SISOOutput(y=y, state=SISOState(ssm=fs, k=fk, v=fv, phi=fphi))

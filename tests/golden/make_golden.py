@@ -112,10 +112,10 @@ def layer_case(tr, name, d_model, d_state, headdim, rope_fraction, b, l, seed):
 
 def main(root):
     tr = _load_torch_ref(root)
-    kernel_case(tr, "recurrent_n16_p8_nr4", b=2, h=3, l=64, n=16, p=8, nr=4, seed=0)
-    kernel_case(tr, "recurrent_n32_p16_nr16", b=1, h=2, l=96, n=32, p=16, nr=16, seed=1)
-    layer_case(tr, "layer_d32_n16_p8", d_model=32, d_state=16, headdim=8, rope_fraction=0.5,
-               b=2, l=64, seed=2)
+    kernel_case(tr, "recurrent_n16_p16_nr4", b=2, h=3, l=128, n=16, p=16, nr=4, seed=0)
+    kernel_case(tr, "recurrent_n32_p16_nr16", b=1, h=2, l=128, n=32, p=16, nr=16, seed=1)
+    layer_case(tr, "layer_d32_n16_p16", d_model=32, d_state=16, headdim=16, rope_fraction=0.5,
+               b=2, l=128, seed=2)
     print("wrote fixtures to", HERE)
 
 

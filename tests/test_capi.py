@@ -1,0 +1,108 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point the header
+declares, the ctypes structs match the C layout, and argument validation rejects bad
+calls with the documented codes before anything reaches a GPU."""
+
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from mamba3_b200 import _capi as C
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "m3_siso.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(m3_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = C.lib()
+    names = _declared()
+    assert set(names) == set(C.EXPORTS)
+    for n in names:
+        assert hasattr(lib, n), n
+    assert lib.m3_version() >= 1
+
+
+def test_struct_layout_matches_header():
+    prog = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "m3_siso.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu\n", sizeof(M3Dims), sizeof(M3Strides), sizeof(M3FwdArgs),
+         sizeof(M3BwdArgs), sizeof(M3DecodeArgs));
+  printf("%zu %zu %zu\n", offsetof(M3FwdArgs, chunk_states_dtype), offsetof(M3BwdArgs, workspace_bytes),
+         offsetof(M3DecodeArgs, y));
+  return 0;
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        open(c, "w").write(prog)
+        subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), c, "-o", exe])
+        out = subprocess.check_output([exe]).decode().split()
+    got = [int(x) for x in out]
+    want = [ctypes.sizeof(C.M3Dims), ctypes.sizeof(C.M3Strides), ctypes.sizeof(C.M3FwdArgs),
+            ctypes.sizeof(C.M3BwdArgs), ctypes.sizeof(C.M3DecodeArgs),
+            C.M3FwdArgs.chunk_states_dtype.offset, C.M3BwdArgs.workspace_bytes.offset, C.M3DecodeArgs.y.offset]
+    assert got == want
+
+
+def _fwd(**kw):
+    a = C.M3FwdArgs()
+    a.dims = C.M3Dims(2, 128, 3, 128, 64, 32, 64)
+    a.io_dtype, a.policy, a.raw = C.M3_DTYPE_F32, C.M3_POLICY_F32, 0
+    fake = 256
+    for f in ("q", "k", "v", "adt", "gamma", "scale", "phi", "q_bias", "k_bias", "y", "final_ssm",
+              "final_k", "final_v"):
+        setattr(a, f, fake)
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("mut,code,frag", [
+    (dict(dims=C.M3Dims(2, 128, 3, 128, 64, 32, 96)), C.M3_ERR_UNSUPPORTED, "chunk"),
+    (dict(dims=C.M3Dims(2, 100, 3, 128, 64, 32, 64)), C.M3_ERR_SHAPE, "multiple of chunk"),
+    (dict(dims=C.M3Dims(2, 128, 3, 128, 64, 80, 64)), C.M3_ERR_SHAPE, "n_angles"),
+    (dict(dims=C.M3Dims(2, 128, 3, 96, 64, 32, 64)), C.M3_ERR_UNSUPPORTED, "state_dim"),
+    (dict(dims=C.M3Dims(0, 128, 3, 128, 64, 32, 64)), C.M3_ERR_SHAPE, "positive"),
+    (dict(q=None), C.M3_ERR_ARG, "required"),
+    (dict(adt=None), C.M3_ERR_ARG, "preprocessed"),
+    (dict(seed_ssm=256), C.M3_ERR_ARG, "together"),
+    (dict(io_dtype=7), C.M3_ERR_ARG, "io_dtype"),
+    (dict(raw=1), C.M3_ERR_ARG, "raw boundary"),
+])
+def test_fwd_validation_errors(mut, code, frag):
+    a = _fwd(**mut)
+    rc = C.lib().m3_siso_fwd(a, None)
+    assert rc == code
+    assert frag in C.lib().m3_last_error().decode()
+
+
+def test_bwd_workspace_validation():
+    a = C.M3BwdArgs()
+    a.dims = C.M3Dims(1, 128, 2, 32, 32, 8, 64)
+    for f in ("q", "k", "v", "adt", "gamma", "scale", "phi", "q_bias", "k_bias", "dy", "dq", "dk", "dv",
+              "dq_bias", "dk_bias", "dadt", "dgamma", "dscale", "dphi"):
+        setattr(a, f, 256)
+    need = C.lib().m3_siso_bwd_workspace_size(ctypes.byref(a.dims))
+    assert need >= 1 * 2 * (128 // 32) * 32 * 32 * 4
+    a.workspace, a.workspace_bytes = 256, need - 1
+    assert C.lib().m3_siso_bwd(a, None) == C.M3_ERR_WORKSPACE
+
+
+def test_decode_validation():
+    a = C.M3DecodeArgs()
+    a.batch, a.nheads, a.state_dim, a.headdim, a.n_angles = 2, 2, 48, 16, 4
+    assert C.lib().m3_siso_decode(a, None) == C.M3_ERR_UNSUPPORTED
+    a.state_dim = 32
+    assert C.lib().m3_siso_decode(a, None) == C.M3_ERR_ARG

@@ -23,7 +23,7 @@ def _load(name):
     return {k: torch.from_numpy(d[k]) for k in d.files}
 
 
-@pytest.mark.parametrize("case", ["recurrent_n16_p8_nr4", "recurrent_n32_p16_nr16"])
+@pytest.mark.parametrize("case", ["recurrent_n16_p16_nr4", "recurrent_n32_p16_nr16"])
 def test_oracle_matches_reference_torch_recurrence(case):
     g = _load(case)
     lam = torch.sigmoid(g["trap"])
@@ -49,7 +49,7 @@ def test_oracle_matches_reference_torch_recurrence(case):
 
 
 def test_oracle_layer_matches_reference_torch_layer():
-    g = _load("layer_d32_n16_p8")
+    g = _load("layer_d32_n16_p16")
     d_model, n, p = int(g["d_model"]), int(g["d_state"]), int(g["headdim"])
     sd = {k[4:].replace("__", "."): v for k, v in g.items() if k.startswith("sd__")}
     perm = O.deinterleave_perm(n)
