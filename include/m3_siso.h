@@ -147,6 +147,20 @@ typedef struct M3BwdArgs {
 size_t m3_siso_bwd_workspace_size(const M3Dims *dims);
 int m3_siso_bwd(const M3BwdArgs *args, void *stream);
 
+/* The same backward for callers that cannot allocate device memory -- a custom call or
+ * plugin that is handed only its inputs and outputs by an allocator it does not own, or
+ * a server that forbids device allocation after start-up.  No counterpart in the
+ * reference (its backward's scratch is XLA-managed VMEM/HBM).  Arguments as for
+ * m3_siso_bwd, except that `workspace` / `workspace_bytes` are ignored: the scratch is a
+ * fixed array inside the library (m3_siso_bwd_noalloc_scratch_bytes() = 64 MiB per
+ * device, resident until exit).  Problems whose m3_siso_bwd_workspace_size() exceeds it
+ * fail with M3_ERR_WORKSPACE.  Nothing is allocated.  All calls on a device share the
+ * array, so calls that overlap on the GPU race and must be serialised by the caller.
+ * The first call on each device resolves the array's address; make it before any stream
+ * capture. */
+int m3_siso_bwd_noalloc(const M3BwdArgs *args, void *stream);
+size_t m3_siso_bwd_noalloc_scratch_bytes(void);
+
 /* ---------------------------------------------------------------------------------
  * Single-token decode step.  Replaces kernel_decode.decode_step / siso_decode /
  * siso_decode_folded (mamba3_pallas/kernel_decode.py:252-471).  The state buffers are

@@ -92,7 +92,7 @@ class M3DecodeArgs(ctypes.Structure):
 
 
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
-           "m3_last_error", "m3_version")
+           "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes")
 
 _lib = None
 
