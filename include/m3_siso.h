@@ -98,7 +98,14 @@ typedef struct M3FwdArgs {
   float *ybar;                          /* optional (B, H, L, P) f32 pre-gate output   */
   void *chunk_states;                   /* optional (B, H, L/chunk, P, N) chunk-start states */
   int32_t chunk_states_dtype;           /* M3_DTYPE_* of chunk_states */
+
+  int32_t kernel;                       /* M3_KERNEL_*: 0 = pick automatically */
 } M3FwdArgs;
+
+/* Kernel selection for m3_siso_fwd.  AUTO uses the tcgen05 tensor-core kernel where it
+ * applies (bf16 I/O, bf16 policy, N = 128, P = 64, chunk % 128 == 0, n_angles <= 64,
+ * 16-byte aligned rows) and the generic CUDA-core kernel otherwise. */
+enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2 };
 
 int m3_siso_fwd(const M3FwdArgs *args, void *stream);
 
@@ -187,6 +194,11 @@ typedef struct M3DecodeArgs {
 } M3DecodeArgs;
 
 int m3_siso_decode(const M3DecodeArgs *args, void *stream);
+
+/* Device-side error word: non-zero if a kernel gave up on a bounded wait for the tensor
+ * core (the kernel then winds down instead of spinning).  Synchronises the device.
+ * `reset` != 0 clears it. */
+int m3_device_error(int reset);
 
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);

@@ -95,6 +95,8 @@ const char* m3_last_error(void) { return g_err.c_str(); }
 
 int m3_version(void) { return 1; }
 
+int m3_device_error(int reset) { return read_device_error(reset); }
+
 int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   g_err.clear();
   if (!args) return set_error(M3_ERR_ARG, "args is NULL");
@@ -114,7 +116,9 @@ int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   def_bhlp(a.y_st, a.dims);
   def_blh(a.raw_st, a.dims);
   def_blx(a.ang_st, a.dims, a.dims.n_angles);
-  return launch_fwd_simt(a, (cudaStream_t)stream);
+  if (a.kernel < M3_KERNEL_AUTO || a.kernel > M3_KERNEL_TENSORCORE)
+    return set_error(M3_ERR_ARG, "kernel must be AUTO, GENERIC or TENSORCORE");
+  return launch_fwd(a, (cudaStream_t)stream);
 }
 
 size_t m3_siso_bwd_workspace_size(const M3Dims* dims) {

@@ -1,0 +1,499 @@
+// Tensor-core (tcgen05 / TMEM) chunked forward for the production shape:
+// bf16 I/O and bf16 matmul operands, N = 128, P = 64, 128-token chunks.
+//
+// One CTA per SM holds two independent "slots" of 256 threads; each slot walks one
+// (b, h) sequence chunk by chunk with its own 112 KB of shared memory and 256 TMEM
+// columns, so while one slot waits on the tensor core the other runs its CUDA-core
+// phases.  Per 128-token chunk (A_t = prefix sum of adt log2 e inside the chunk):
+//
+//   CUDA cores : per-token dt / A / lambda / gamma / scale (fused preprocess), the
+//                cumulative rotary angles, rotation of q and k (bf16 q~, khat = k~ scale
+//                into SWIZZLE_128B K-major tiles), v and v exp2(A_last - A) tiles
+//   tcgen05    : S = q~ khat^T            (128 x 128, K = N)    -> TMEM [0, 128)
+//                Yi = q~ St^T             (128 x 64,  K = N)    -> TMEM [128, 192)
+//                dSt = khat^T vd          (128 x 64,  K = 128)  -> TMEM [192, 256)
+//   CUDA cores : St <- exp2(A_last) St + dSt (fp32, registers), bf16 copy for the next
+//                chunk's readout; decay mask of S -> bf16 into the q~ tile
+//   tcgen05    : Ya = mask(S) v           (128 x 64,  K = 128)  -> TMEM [0, 64)
+//   CUDA cores : y = exp2(A) Yi + Ya + (D + gamma u.w) v, times silu(z), store.
+//
+// This is kernel_fwd.py:55-201 of the reference (the same bf16 rounding points:
+// kernel_fwd.py:139-187) with reference.py:104-199's preprocessing fused in.  Every
+// wait on the tensor core is bounded; a time-out records an error in g_m3_device_error
+// and the slot winds down instead of spinning.
+#pragma once
+
+#include "m3_chunk_common.cuh"
+#include "m3_umma.cuh"
+
+namespace m3 {
+
+__device__ int g_m3_device_error;  // non-zero after a bounded wait gave up
+
+namespace tc {
+
+constexpr int kN = 128, kP = 64, kC = 128;
+constexpr int kSlotThreads = 256;
+constexpr int kThreads = 2 * kSlotThreads;
+constexpr uint32_t kQ = 0, kK = 32768, kV = 65536, kVd = 81920, kSt = 98304, kSlotBytes = 114688;
+// scratch laid over the vd tile while it is not live
+constexpr uint32_t kScrDt = 0, kScrScl = 512, kScrSeg = 1024, kScrUw = 3072, kScrA = 0;
+
+struct SlotSmall {
+  uint64_t mbar[2];
+  float wtot[4];
+  float carry[64];
+};
+struct CtaSmall {
+  SlotSmall slot[2];
+  uint32_t tmem;
+};
+constexpr size_t kSmemBytes = 2 * (size_t)kSlotBytes + sizeof(CtaSmall) + 1024;  // + alignment slack
+
+__device__ __forceinline__ void slot_sync(int slot) {
+  asm volatile("bar.sync %0, %1;" ::"r"(slot + 1), "r"(kSlotThreads) : "memory");
+}
+
+// Barrier over the slot's threads that also ORs `pred` across them, so a decision taken
+// after a bounded wait is the same in every thread of the slot.
+__device__ __forceinline__ bool slot_any(int slot, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %2, 0;\n\t"
+      "bar.red.or.pred p, %1, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"(slot + 1), "r"((uint32_t)pred), "r"(kSlotThreads)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
+
+// sin / cos of an angle in [0, 2 pi) through the SFU (accurate on [-pi, pi]).
+__device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
+  if (x >= kPi) x -= kTwoPi;
+  __sincosf(x, s, c);
+}
+
+// tanh from exp2 and a reciprocal: |error| ~ 1e-7 absolute and unbiased, so the
+// cumulative angle does not drift (tanh.approx's 2^-11 relative error would).
+__device__ __forceinline__ float tanh_acc(float x) {
+  const float e = exp2f(2.f * kLog2e * fminf(fabsf(x), 15.f));
+  const float t = 1.f - 2.f / (e + 1.f);
+  return copysignf(t, x);
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  u.x = umma::pack_bf16x2(f[0], f[1]);
+  u.y = umma::pack_bf16x2(f[2], f[3]);
+  u.z = umma::pack_bf16x2(f[4], f[5]);
+  u.w = umma::pack_bf16x2(f[6], f[7]);
+  return u;
+}
+
+template <bool RAW>
+__global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) {
+  extern __shared__ uint8_t smraw[];
+  uint8_t* base = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  CtaSmall* cs = (CtaSmall*)(base + 2 * kSlotBytes);
+  const int slot = threadIdx.x / kSlotThreads;
+  const int ltid = threadIdx.x % kSlotThreads;
+  const int lwarp = ltid >> 5, lane = ltid & 31;
+  uint8_t* sm = base + slot * kSlotBytes;
+  SlotSmall* ss = &cs->slot[slot];
+  const int H = a.dims.nheads, L = a.dims.seqlen, Nr = a.dims.n_angles;
+  const int nseq = a.dims.batch * H;
+  const int seq = blockIdx.x * 2 + slot;
+  const bool active = seq < nseq;
+
+  if (threadIdx.x < 32) umma::tmem_alloc(&cs->tmem, 512);
+  if (ltid == 0) {
+    umma::mbar_init(&ss->mbar[0], 1);
+    umma::mbar_init(&ss->mbar[1], 1);
+    umma::fence_mbar_init();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tm = cs->tmem + (uint32_t)slot * 256u;
+
+  if (active) {
+    const int b = seq / H, h = seq % H;
+    const size_t bh = (size_t)seq;
+    const int t = ltid & 127, half = ltid >> 7;    // token row / state row, column half
+    const int rp = lane, sg = lwarp;               // angle pair (2 rp, 2 rp + 1), 16-token segment
+    const uint32_t lane_base = (uint32_t)(32 * (lwarp & 3)) << 16;
+    const __nv_bfloat16* q = (const __nv_bfloat16*)a.q;
+    const __nv_bfloat16* k = (const __nv_bfloat16*)a.k;
+    const __nv_bfloat16* v = (const __nv_bfloat16*)a.v;
+    const __nv_bfloat16* z = (const __nv_bfloat16*)a.z;
+    __nv_bfloat16* y = (__nv_bfloat16*)a.y;
+    const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
+    const int nchunk = L / kC;
+    const int chunk_sub = a.dims.chunk / kC;
+    const uint32_t sQ = umma::smem_u32(sm + kQ), sK = umma::smem_u32(sm + kK), sV = umma::smem_u32(sm + kV);
+    const uint32_t sVd = umma::smem_u32(sm + kVd), sSt = umma::smem_u32(sm + kSt);
+    bool ok = true;
+
+    // per-thread bias pairs for the rotation role: columns 2rp, 2rp+1 (lo) and +64 (hi)
+    const float2 qbl = *reinterpret_cast<const float2*>(a.q_bias + h * kN + 2 * rp);
+    const float2 qbh = *reinterpret_cast<const float2*>(a.q_bias + h * kN + 64 + 2 * rp);
+    const float2 kbl = *reinterpret_cast<const float2*>(a.k_bias + h * kN + 2 * rp);
+    const float2 kbh = *reinterpret_cast<const float2*>(a.k_bias + h * kN + 64 + 2 * rp);
+
+    // ---- initial state: registers hold St[n = t][p = 32 half + i] (fp32) ------------
+    float st[32];
+    {
+      float coef = 0.f;
+      if (a.seed_ssm) {
+        if (RAW) {
+          const size_t o = (size_t)b * a.raw_st.b + (size_t)h * a.raw_st.h;
+          coef = softplusf(a.dt_raw[o] + a.dt_bias[h]) * (1.f - sigmoidf_(a.trap_raw[o]));
+        } else {
+          coef = a.seed_coef[bh];
+        }
+      }
+      const float kprev = a.seed_ssm ? a.seed_k[bh * kN + t] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int p = 32 * half + i;
+        st[i] = a.seed_ssm ? a.seed_ssm[(bh * kP + p) * kN + t] + coef * a.seed_v[bh * kP + p] * kprev : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(st + 8 * j);
+      if (RAW && ltid < 64) ss->carry[ltid] = (a.seed_phi && ltid < Nr) ? a.seed_phi[bh * Nr + ltid] : 0.f;
+    }
+    slot_sync(slot);
+
+    for (int c = 0; c < nchunk && ok; ++c) {
+      const int t0 = c * kC;
+      const int tg = t0 + t;  // this thread's token (row roles)
+      // ---- phase 1: per-token scalars ------------------------------------------------
+      float dt = 0.f, adt, gam, scl;
+      if (RAW) {
+        const size_t o = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
+        dt = softplusf(a.dt_raw[o] + a.dt_bias[h]);
+        const float lam = sigmoidf_(a.trap_raw[o]);
+        adt = fminf(-heavy_tail(a.a_raw[o]), -a.a_floor) * dt;
+        float dtn = __shfl_down_sync(0xffffffffu, dt, 1), lamn = __shfl_down_sync(0xffffffffu, lam, 1);
+        if (lane == 31) {  // the successor lives in the next warp or the next chunk
+          dtn = lamn = 0.f;
+          if (tg + 1 < L) {
+            const size_t on = o + a.raw_st.l;
+            dtn = softplusf(a.dt_raw[on] + a.dt_bias[h]);
+            lamn = sigmoidf_(a.trap_raw[on]);
+          }
+        }
+        gam = dt * lam;
+        scl = gam + dtn * (1.f - lamn);
+      } else {
+        const size_t o = bh * L + tg;
+        adt = a.adt[o];
+        gam = a.gamma[o];
+        scl = a.scale[o];
+      }
+      const float incl = warp_inclusive_scan(adt * kLog2e);
+      if (half == 0 && lane == 31) ss->wtot[lwarp & 3] = incl;
+      if (half == 0) {
+        if (RAW) reinterpret_cast<float*>(sm + kVd + kScrDt)[t] = dt;
+        reinterpret_cast<float*>(sm + kVd + kScrScl)[t] = scl;
+      }
+      slot_sync(slot);
+      float A = incl;
+      for (int w = 0; w < (lwarp & 3); ++w) A += ss->wtot[w];
+      const float Alast = ss->wtot[0] + ss->wtot[1] + ss->wtot[2] + ss->wtot[3];
+
+      // ---- phase 2: cumulative angles, rotation ---------------------------------------
+      {
+        const float* dts = reinterpret_cast<const float*>(sm + kVd + kScrDt);
+        const float* scls = reinterpret_cast<const float*>(sm + kVd + kScrScl);
+        float* segtot = reinterpret_cast<float*>(sm + kVd + kScrSeg);  // [8][64]
+        const int r0 = 2 * rp;
+        const bool rot0 = r0 < Nr, rot1 = r0 + 1 < Nr;
+        float th0[16], th1[16];
+        float off0 = 0.f, off1 = 0.f;
+        if (RAW) {
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int tt = sg * 16 + i;
+            float2 an = make_float2(0.f, 0.f);
+            const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tt) * a.ang_st.l + r0;
+            if (rot1) an = *reinterpret_cast<const float2*>(ap);
+            else if (rot0) an.x = ap[0];
+            const float w = kPi * dts[tt];
+            th0[i] = rot0 ? tanh_acc(an.x) * w : 0.f;
+            th1[i] = rot1 ? tanh_acc(an.y) * w : 0.f;
+            s0 += th0[i];
+            s1 += th1[i];
+          }
+          segtot[sg * 64 + r0] = s0;
+          segtot[sg * 64 + r0 + 1] = s1;
+          slot_sync(slot);
+          off0 = rot0 ? ss->carry[r0] : 0.f;
+          off1 = rot1 ? ss->carry[r0 + 1] : 0.f;
+          for (int g = 0; g < sg; ++g) {
+            off0 += segtot[g * 64 + r0];
+            off1 += segtot[g * 64 + r0 + 1];
+          }
+        }
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int tt = sg * 16 + i, tgl = t0 + tt;
+          float c0 = 1.f, s0 = 0.f, c1 = 1.f, s1 = 0.f;
+          if (RAW) {
+            off0 += th0[i];
+            off1 += th1[i];
+            if (rot0) sincos_wrapped(wrap2pi(off0), &s0, &c0);
+            if (rot1) sincos_wrapped(wrap2pi(off1), &s1, &c1);
+          } else {
+            const float* pp = a.phi + (bh * L + tgl) * Nr + r0;
+            if (rot0) sincos_wrapped(wrap2pi(pp[0]), &s0, &c0);
+            if (rot1) sincos_wrapped(wrap2pi(pp[1]), &s1, &c1);
+          }
+          const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tgl * a.q_st.l;
+          const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tgl * a.k_st.l;
+          const uint32_t uq_lo = *reinterpret_cast<const uint32_t*>(qr + r0);
+          const uint32_t uq_hi = *reinterpret_cast<const uint32_t*>(qr + 64 + r0);
+          const uint32_t uk_lo = *reinterpret_cast<const uint32_t*>(kr + r0);
+          const uint32_t uk_hi = *reinterpret_cast<const uint32_t*>(kr + 64 + r0);
+          const float ul0 = bf16lo(uq_lo) + qbl.x, ul1 = bf16hi(uq_lo) + qbl.y;
+          const float uh0 = bf16lo(uq_hi) + qbh.x, uh1 = bf16hi(uq_hi) + qbh.y;
+          const float wl0 = bf16lo(uk_lo) + kbl.x, wl1 = bf16hi(uk_lo) + kbl.y;
+          const float wh0 = bf16lo(uk_hi) + kbh.x, wh1 = bf16hi(uk_hi) + kbh.y;
+          const float ql0 = ul0 * c0 - uh0 * s0, qh0 = uh0 * c0 + ul0 * s0;
+          const float ql1 = ul1 * c1 - uh1 * s1, qh1 = uh1 * c1 + ul1 * s1;
+          const float kl0 = wl0 * c0 - wh0 * s0, kh0 = wh0 * c0 + wl0 * s0;
+          const float kl1 = wl1 * c1 - wh1 * s1, kh1 = wh1 * c1 + wl1 * s1;
+          const float sc = scls[tt];
+          // element (row tt, col k) of a K-major SW128 tile pair: k / 64 picks the
+          // 16 KB block, (k % 64) / 8 the 16-byte chunk, k % 8 the bf16 inside it
+          const uint32_t col_lo = umma::sw128_off(tt, r0 >> 3) + (r0 & 7) * 2;
+          *reinterpret_cast<uint32_t*>(sm + kQ + col_lo) = umma::pack_bf16x2(ql0, ql1);
+          *reinterpret_cast<uint32_t*>(sm + kQ + 16384 + col_lo) = umma::pack_bf16x2(qh0, qh1);
+          *reinterpret_cast<uint32_t*>(sm + kK + col_lo) = umma::pack_bf16x2(kl0 * sc, kl1 * sc);
+          *reinterpret_cast<uint32_t*>(sm + kK + 16384 + col_lo) = umma::pack_bf16x2(kh0 * sc, kh1 * sc);
+          if (tgl == L - 1) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
+            float* fk = a.final_k + bh * kN;
+            fk[r0] = kl0;
+            fk[r0 + 1] = kl1;
+            fk[64 + r0] = kh0;
+            fk[64 + r0 + 1] = kh1;
+          }
+        }
+      }
+      // u.w for the diagonal term: each half sums 64 of the N columns of its token
+      {
+        const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tg * a.q_st.l + 64 * half;
+        const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tg * a.k_st.l + 64 * half;
+        const float* qb = a.q_bias + h * kN + 64 * half;
+        const float* kb = a.k_bias + h * kN + 64 * half;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 uq = *reinterpret_cast<const uint4*>(qr + 8 * j);
+          const uint4 uk = *reinterpret_cast<const uint4*>(kr + 8 * j);
+          const uint32_t qa[4] = {uq.x, uq.y, uq.z, uq.w}, ka[4] = {uk.x, uk.y, uk.z, uk.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = 8 * j + 2 * e;
+            acc += (bf16lo(qa[e]) + qb[n]) * (bf16lo(ka[e]) + kb[n]);
+            acc += (bf16hi(qa[e]) + qb[n + 1]) * (bf16hi(ka[e]) + kb[n + 1]);
+          }
+        }
+        reinterpret_cast<float*>(sm + kVd + kScrUw)[half * 128 + t] = acc;
+      }
+      slot_sync(slot);
+      float dg;
+      {
+        const float* uwp = reinterpret_cast<const float*>(sm + kVd + kScrUw);
+        dg = (uwp[t] + uwp[128 + t]) * gam + Dh;
+      }
+      if (RAW && ltid < 64) {
+        const float* segtot = reinterpret_cast<const float*>(sm + kVd + kScrSeg);
+        float tot = ss->carry[ltid];
+        for (int g = 0; g < 8; ++g) tot += segtot[g * 64 + ltid];
+        ss->carry[ltid] = wrap2pi(tot);
+      }
+      slot_sync(slot);
+
+      // ---- phase 3: v and v exp2(A_last - A) tiles (MN-major: row = token) -------------
+      uint32_t vreg[16];  // this thread's 32 v values (bf16 pairs), kept for the diagonal term
+      {
+        const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)tg * a.v_st.l + 32 * half;
+        const float e = exp2f(Alast - A);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 u = *reinterpret_cast<const uint4*>(vr + 8 * j);
+          vreg[4 * j + 0] = u.x;
+          vreg[4 * j + 1] = u.y;
+          vreg[4 * j + 2] = u.z;
+          vreg[4 * j + 3] = u.w;
+          *reinterpret_cast<uint4*>(sm + kV + umma::sw128_off(t, 4 * half + j)) = u;
+          uint4 d;
+          d.x = umma::pack_bf16x2(bf16lo(u.x) * e, bf16hi(u.x) * e);
+          d.y = umma::pack_bf16x2(bf16lo(u.y) * e, bf16hi(u.y) * e);
+          d.z = umma::pack_bf16x2(bf16lo(u.z) * e, bf16hi(u.z) * e);
+          d.w = umma::pack_bf16x2(bf16lo(u.w) * e, bf16hi(u.w) * e);
+          *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + j)) = d;
+        }
+      }
+      umma::fence_async_smem();
+      umma::fence_before_sync();
+      slot_sync(slot);
+      umma::fence_after_sync();
+
+      // ---- phase 4: S, Yi, dSt on the tensor core ----------------------------------------
+      if (ltid == 0) {
+        constexpr uint32_t id_s = umma::idesc_bf16(128, 128, false, false);
+        constexpr uint32_t id_yi = umma::idesc_bf16(128, 64, false, true);
+        constexpr uint32_t id_ds = umma::idesc_bf16(128, 64, true, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
+          const uint32_t mn = ks * 2048u;
+          const uint64_t dq = umma::smem_desc(sQ + kmaj, 16, 1024);
+          umma::mma_bf16(tm + 0, dq, umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
+          umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + mn, 16384, 1024), id_yi, ks > 0);
+          umma::mma_bf16(tm + 192, umma::smem_desc(sK + mn, 16384, 1024), umma::smem_desc(sVd + mn, 16384, 1024),
+                         id_ds, ks > 0);
+        }
+        umma::commit(&ss->mbar[0]);
+      }
+      if (slot_any(slot, !umma::mbar_wait(&ss->mbar[0], c & 1))) {
+        if (ltid == 0) atomicExch(&g_m3_device_error, 1);
+        ok = false;
+        break;
+      }
+      umma::fence_after_sync();
+
+      // ---- phase 5a: state update (St lane n = t, columns 32 half ..) ---------------------
+      {
+        if (a.chunk_states && c % chunk_sub == 0) {
+          const int nc = L / a.dims.chunk, ci = c / chunk_sub;
+          const size_t sb = ((bh * nc + ci) * kP) * kN;
+#pragma unroll 8
+          for (int i = 0; i < 32; ++i) {
+            const size_t o = sb + (size_t)(32 * half + i) * kN + t;
+            if (a.chunk_states_dtype == M3_DTYPE_BF16) ((__nv_bfloat16*)a.chunk_states)[o] = __float2bfloat16_rn(st[i]);
+            else ((float*)a.chunk_states)[o] = st[i];
+          }
+        }
+        float d[32];
+        umma::tmem_ld32(tm + lane_base + 192 + 32 * half, d);
+        umma::tmem_wait_ld();
+        const float eAl = exp2f(Alast);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) st[i] = st[i] * eAl + d[i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(st + 8 * j);
+        if (half == 0) reinterpret_cast<float*>(sm + kVd + kScrA)[t] = A;
+      }
+      slot_sync(slot);
+      // ---- phase 5b: decay mask of S -> bf16 into the q~ tile -----------------------------
+      {
+        const float* As = reinterpret_cast<const float*>(sm + kVd + kScrA);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+          float sv[32];
+          const int sb = 64 * half + 32 * cb;
+          const bool any = sb < t;
+          umma::tmem_ld32(tm + lane_base + sb, sv);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float m[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int s = sb + 8 * j + e;
+              m[e] = (any && s < t) ? sv[8 * j + e] * exp2f(fminf(A - As[s], 0.f)) : 0.f;
+            }
+            *reinterpret_cast<uint4*>(sm + kQ + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(m);
+          }
+        }
+      }
+      umma::fence_async_smem();
+      umma::fence_before_sync();
+      slot_sync(slot);
+      umma::fence_after_sync();
+      if (ltid == 0) {
+        constexpr uint32_t id_ya = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
+          umma::mma_bf16(tm + 0, umma::smem_desc(sQ + kmaj, 16, 1024), umma::smem_desc(sV + ks * 2048u, 16384, 1024),
+                         id_ya, ks > 0);
+        }
+        umma::commit(&ss->mbar[1]);
+      }
+      if (slot_any(slot, !umma::mbar_wait(&ss->mbar[1], c & 1))) {
+        if (ltid == 0) atomicExch(&g_m3_device_error, 2);
+        ok = false;
+        break;
+      }
+      umma::fence_after_sync();
+
+      // ---- phase 6: output -----------------------------------------------------------------
+      {
+        float yi[32], ya[32];
+        umma::tmem_ld32(tm + lane_base + 128 + 32 * half, yi);
+        umma::tmem_ld32(tm + lane_base + 32 * half, ya);
+        umma::tmem_wait_ld();
+        const float eA = exp2f(A);
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o[2 * i] = eA * yi[2 * i] + ya[2 * i] + dg * bf16lo(vreg[i]);
+          o[2 * i + 1] = eA * yi[2 * i + 1] + ya[2 * i + 1] + dg * bf16hi(vreg[i]);
+        }
+        if (a.ybar) {
+          float* yb = a.ybar + (bh * L + tg) * kP + 32 * half;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yb + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+        }
+        if (z) {
+          const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(zr + 8 * j);
+            const uint32_t zz[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float z0 = bf16lo(zz[e]), z1 = bf16hi(zz[e]);
+              o[8 * j + 2 * e] *= z0 * sigmoidf_(z0);
+              o[8 * j + 2 * e + 1] *= z1 * sigmoidf_(z1);
+            }
+          }
+        }
+        __nv_bfloat16* yr = y + (size_t)b * a.y_st.b + (size_t)h * a.y_st.h + (size_t)tg * a.y_st.l + 32 * half;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(yr + 8 * j) = pack8(o + 8 * j);
+      }
+      umma::fence_before_sync();
+      slot_sync(slot);
+      umma::fence_after_sync();
+    }
+
+    // ---- final state (kernel_fwd.py:189-201) ---------------------------------------------
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = st[i];
+    if (ltid < kP) {
+      const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(L - 1) * a.v_st.l;
+      a.final_v[bh * kP + ltid] = __bfloat162float(vr[ltid]);
+    }
+    if (a.final_phi && ltid < Nr)
+      a.final_phi[bh * Nr + ltid] = RAW ? ss->carry[ltid] : a.phi[(bh * L + L - 1) * Nr + ltid];
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x < 32) umma::tmem_dealloc(cs->tmem, 512);
+}
+
+}  // namespace tc
+}  // namespace m3

@@ -17,7 +17,8 @@ int check_launch(const char* what);
 // Supported (N, P) pairs of the generic kernels.
 bool supported_np(int n, int p);
 
-int launch_fwd_simt(const M3FwdArgs& a, cudaStream_t s);
+int launch_fwd(const M3FwdArgs& a, cudaStream_t s);
+int read_device_error(int reset);
 int launch_bwd_simt(const M3BwdArgs& a, cudaStream_t s);
 int launch_decode(const M3DecodeArgs& a, cudaStream_t s);
 size_t bwd_workspace_bytes(const M3Dims& d);

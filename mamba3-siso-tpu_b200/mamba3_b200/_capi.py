@@ -52,7 +52,13 @@ class M3FwdArgs(ctypes.Structure):
         ("y", _vp), ("y_st", M3Strides),
         ("final_ssm", _vp), ("final_k", _vp), ("final_v", _vp), ("final_phi", _vp),
         ("ybar", _vp), ("chunk_states", _vp), ("chunk_states_dtype", _i32),
+        ("kernel", _i32),
     ]
+
+
+M3_KERNEL_AUTO = 0
+M3_KERNEL_GENERIC = 1
+M3_KERNEL_TENSORCORE = 2
 
 
 class M3BwdArgs(ctypes.Structure):
@@ -92,7 +98,8 @@ class M3DecodeArgs(ctypes.Structure):
 
 
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
-           "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes")
+           "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
+           "m3_device_error")
 
 _lib = None
 
@@ -118,6 +125,8 @@ def lib():
         L.m3_last_error.restype = ctypes.c_char_p
         L.m3_version.argtypes = []
         L.m3_version.restype = ctypes.c_int
+        L.m3_device_error.argtypes = [ctypes.c_int]
+        L.m3_device_error.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -24,6 +24,14 @@ class ForwardResiduals(NamedTuple):
     chunk_states: torch.Tensor
 
 
+def _kernel_code(kernel: str) -> int:
+    """``"auto"`` (tensor cores where they apply), ``"generic"`` or ``"tensorcore"``."""
+    codes = {"auto": C.M3_KERNEL_AUTO, "generic": C.M3_KERNEL_GENERIC, "tensorcore": C.M3_KERNEL_TENSORCORE}
+    if kernel not in codes:
+        raise ValueError(f"kernel must be one of {sorted(codes)}, got {kernel!r}")
+    return codes[kernel]
+
+
 def _dims(q, v, n_angles, chunk) -> C.M3Dims:
     b, l, n = q.shape
     return C.M3Dims(b, l, v.shape[1], n, v.shape[3], n_angles, chunk)
@@ -41,7 +49,7 @@ def _check_shapes(q, k, v, z):
 
 def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z=None,
                  seed_ssm=None, seed_k=None, seed_v=None, seed_coef=None, chunk: int = 128,
-                 dtype_policy: str = "bf16", save_residuals: bool = False, out_y=None):
+                 dtype_policy: str = "bf16", save_residuals: bool = False, out_y=None, kernel: str = "auto"):
     """Chunked forward at the preprocessed boundary.
 
     Returns ``(y, final_ssm, final_k, final_v)`` and `ForwardResiduals` when
@@ -94,6 +102,7 @@ def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z
     if save_residuals:
         a.ybar, a.chunk_states = T.ptr(ybar), T.ptr(states)
         a.chunk_states_dtype = T.io_dtype(states.dtype)
+    a.kernel = _kernel_code(kernel)
     C.check(C.lib().m3_siso_fwd(a, T.stream_handle(dev)))
     if save_residuals:
         return y, fs, fk, fv, ForwardResiduals(ybar=ybar, chunk_states=states)
@@ -103,7 +112,7 @@ def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z
 def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias,
                      d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                      a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
-                     y_out: Optional[torch.Tensor] = None):
+                     y_out: Optional[torch.Tensor] = None, kernel: str = "auto"):
     """Fused boundary: raw ``(B, L, H)`` dt/A/trap streams and head-shared ``(B, L, Nr)``
     angles (all may be strided views of an in_proj output).  Returns
     ``(y, final_ssm, final_k, final_v, final_phi)``.  ``y_out`` may be a strided
@@ -149,5 +158,6 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     a.seed_ssm, a.seed_k, a.seed_v, a.seed_phi = T.ptr(s_ssm), T.ptr(s_k), T.ptr(s_v), T.ptr(s_phi)
     a.y, a.y_st = T.ptr(y), T.st_bhlp(y)
     a.final_ssm, a.final_k, a.final_v, a.final_phi = T.ptr(fs), T.ptr(fk), T.ptr(fv), T.ptr(fphi)
+    a.kernel = _kernel_code(kernel)
     C.check(C.lib().m3_siso_fwd(a, T.stream_handle(dev)))
     return y, fs, fk, fv, fphi
