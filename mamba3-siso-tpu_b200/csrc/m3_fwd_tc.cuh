@@ -30,6 +30,23 @@ namespace m3 {
 
 __device__ int g_m3_device_error;  // non-zero after a bounded wait gave up
 
+#ifdef M3_TC_TIMING
+// Per-phase cycle totals of slot-thread 0 of every slot (diagnostic builds only).
+__device__ unsigned long long g_m3_tc_timing[8];
+#define M3_TC_MARK(i)                                                   \
+  do {                                                                  \
+    if (ltid == 0) {                                                    \
+      const long long now_ = clock64();                                 \
+      atomicAdd(&g_m3_tc_timing[i], (unsigned long long)(now_ - tmark_)); \
+      tmark_ = now_;                                                    \
+    }                                                                   \
+  } while (0)
+#else
+#define M3_TC_MARK(i) \
+  do {                \
+  } while (0)
+#endif
+
 namespace tc {
 
 constexpr int kN = 128, kP = 64, kC = 128;
@@ -78,13 +95,28 @@ __device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
   __sincosf(x, s, c);
 }
 
-// tanh from exp2 and a reciprocal: |error| ~ 1e-7 absolute and unbiased, so the
-// cumulative angle does not drift (tanh.approx's 2^-11 relative error would).
+// 2^x on the SFU (relative error ~2^-22; flushes subnormal results to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// phi - 2 pi floor(phi / 2 pi) with a reciprocal multiply instead of a division.
+__device__ __forceinline__ float wrap_fast(float x) {
+  return x - kTwoPi * floorf(x * 0.15915494309189535f);
+}
+
+// tanh from exp2 and a correctly rounded reciprocal: |error| ~ 1e-7 absolute and
+// unbiased, so the cumulative angle does not drift (tanh.approx's 2^-11 would).
 __device__ __forceinline__ float tanh_acc(float x) {
-  const float e = exp2f(2.f * kLog2e * fminf(fabsf(x), 15.f));
-  const float t = 1.f - 2.f / (e + 1.f);
+  const float e = ex2(2.f * kLog2e * fminf(fabsf(x), 15.f));
+  const float t = 1.f - 2.f * __frcp_rn(e + 1.f);
   return copysignf(t, x);
 }
+
+// z sigmoid(z) for the output gate (bf16 output: the SFU exp and reciprocal suffice).
+__device__ __forceinline__ float silu_fast(float z) { return z * __frcp_rn(1.f + __expf(-z)); }
 
 __device__ __forceinline__ uint4 pack8(const float* f) {
   uint4 u;
@@ -170,32 +202,85 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
     }
     slot_sync(slot);
 
+    // Raw q / k rows of chunk `cc` straight into the q~ / khat tiles (K-major, swizzled)
+    // and its v rows into the v tile (MN-major); rotated / scaled in place afterwards.
+    auto prefetch_qv = [&](int cc) {
+      const int tb = cc * kC;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int i = ltid + kSlotThreads * m;  // 0 .. 2047
+        const int row = i >> 4, c16 = i & 15;
+        const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
+        umma::cp_async16(sQ + dst, q + (size_t)b * a.q_st.b + (size_t)(tb + row) * a.q_st.l + c16 * 8);
+      }
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i = ltid + kSlotThreads * m;  // 0 .. 1023
+        const int row = i >> 3, c8 = i & 7;
+        umma::cp_async16(sV + umma::sw128_off(row, c8),
+                         v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(tb + row) * a.v_st.l + c8 * 8);
+      }
+      umma::cp_async_commit();
+    };
+    auto prefetch_k = [&](int cc) {
+      const int tb = cc * kC;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int i = ltid + kSlotThreads * m;
+        const int row = i >> 4, c16 = i & 15;
+        const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
+        umma::cp_async16(sK + dst, k + (size_t)b * a.k_st.b + (size_t)(tb + row) * a.k_st.l + c16 * 8);
+      }
+      umma::cp_async_commit();
+    };
+    prefetch_qv(0);
+    prefetch_k(0);
+    // raw per-token scalars of chunk `cc` for this thread's token row
+    const float dtb = RAW ? a.dt_bias[h] : 0.f;
+    float rs[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+    auto load_scalars = [&](int cc) {
+      const int tt = cc * kC + t;
+      if (RAW) {
+        const size_t o = (size_t)b * a.raw_st.b + (size_t)tt * a.raw_st.l + (size_t)h * a.raw_st.h;
+        rs[0] = a.dt_raw[o];
+        rs[1] = a.a_raw[o];
+        rs[2] = a.trap_raw[o];
+        if (lane == 31 && tt + 1 < L) {
+          rs[3] = a.dt_raw[o + a.raw_st.l];
+          rs[4] = a.trap_raw[o + a.raw_st.l];
+        }
+      } else {
+        const size_t o = bh * L + tt;
+        rs[0] = a.adt[o];
+        rs[1] = a.gamma[o];
+        rs[2] = a.scale[o];
+      }
+    };
+    load_scalars(0);
+
+#ifdef M3_TC_TIMING
+    long long tmark_ = clock64();
+#endif
     for (int c = 0; c < nchunk && ok; ++c) {
       const int t0 = c * kC;
       const int tg = t0 + t;  // this thread's token (row roles)
-      // ---- phase 1: per-token scalars ------------------------------------------------
+      // ---- phase 1: per-token scalars (raw values were loaded during the last chunk) ---
       float dt = 0.f, adt, gam, scl;
       if (RAW) {
-        const size_t o = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
-        dt = softplusf(a.dt_raw[o] + a.dt_bias[h]);
-        const float lam = sigmoidf_(a.trap_raw[o]);
-        adt = fminf(-heavy_tail(a.a_raw[o]), -a.a_floor) * dt;
+        dt = softplusf(rs[0] + dtb);
+        const float lam = sigmoidf_(rs[2]);
+        adt = fminf(-heavy_tail(rs[1]), -a.a_floor) * dt;
         float dtn = __shfl_down_sync(0xffffffffu, dt, 1), lamn = __shfl_down_sync(0xffffffffu, lam, 1);
         if (lane == 31) {  // the successor lives in the next warp or the next chunk
-          dtn = lamn = 0.f;
-          if (tg + 1 < L) {
-            const size_t on = o + a.raw_st.l;
-            dtn = softplusf(a.dt_raw[on] + a.dt_bias[h]);
-            lamn = sigmoidf_(a.trap_raw[on]);
-          }
+          dtn = tg + 1 < L ? softplusf(rs[3] + dtb) : 0.f;
+          lamn = tg + 1 < L ? sigmoidf_(rs[4]) : 0.f;
         }
         gam = dt * lam;
         scl = gam + dtn * (1.f - lamn);
       } else {
-        const size_t o = bh * L + tg;
-        adt = a.adt[o];
-        gam = a.gamma[o];
-        scl = a.scale[o];
+        adt = rs[0];
+        gam = rs[1];
+        scl = rs[2];
       }
       const float incl = warp_inclusive_scan(adt * kLog2e);
       if (half == 0 && lane == 31) ss->wtot[lwarp & 3] = incl;
@@ -203,10 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
         if (RAW) reinterpret_cast<float*>(sm + kVd + kScrDt)[t] = dt;
         reinterpret_cast<float*>(sm + kVd + kScrScl)[t] = scl;
       }
+      umma::cp_async_wait_all();  // this chunk's q / k / v rows have landed
       slot_sync(slot);
       float A = incl;
       for (int w = 0; w < (lwarp & 3); ++w) A += ss->wtot[w];
       const float Alast = ss->wtot[0] + ss->wtot[1] + ss->wtot[2] + ss->wtot[3];
+      M3_TC_MARK(0);
 
       // ---- phase 2: cumulative angles, rotation ---------------------------------------
       {
@@ -219,22 +306,26 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
         float off0 = 0.f, off1 = 0.f;
         if (RAW) {
           float s0 = 0.f, s1 = 0.f;
+          // every load first (in-row column indices, so always in bounds), then the math
+          const int c0i = min(r0, Nr - 1), c1i = min(r0 + 1, Nr - 1);
+          const float* abase = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + sg * 16) * a.ang_st.l;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const int tt = sg * 16 + i;
-            float2 an = make_float2(0.f, 0.f);
-            const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tt) * a.ang_st.l + r0;
-            if (rot1) an = *reinterpret_cast<const float2*>(ap);
-            else if (rot0) an.x = ap[0];
-            const float w = kPi * dts[tt];
-            th0[i] = rot0 ? tanh_acc(an.x) * w : 0.f;
-            th1[i] = rot1 ? tanh_acc(an.y) * w : 0.f;
+            th0[i] = abase[(size_t)i * a.ang_st.l + c0i];
+            th1[i] = abase[(size_t)i * a.ang_st.l + c1i];
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float w = kPi * dts[sg * 16 + i];
+            th0[i] = rot0 ? tanh_acc(th0[i]) * w : 0.f;
+            th1[i] = rot1 ? tanh_acc(th1[i]) * w : 0.f;
             s0 += th0[i];
             s1 += th1[i];
           }
           segtot[sg * 64 + r0] = s0;
           segtot[sg * 64 + r0 + 1] = s1;
           slot_sync(slot);
+          M3_TC_MARK(7);
           off0 = rot0 ? ss->carry[r0] : 0.f;
           off1 = rot1 ? ss->carry[r0 + 1] : 0.f;
           for (int g = 0; g < sg; ++g) {
@@ -249,19 +340,18 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
           if (RAW) {
             off0 += th0[i];
             off1 += th1[i];
-            if (rot0) sincos_wrapped(wrap2pi(off0), &s0, &c0);
-            if (rot1) sincos_wrapped(wrap2pi(off1), &s1, &c1);
+            if (rot0) sincos_wrapped(wrap_fast(off0), &s0, &c0);
+            if (rot1) sincos_wrapped(wrap_fast(off1), &s1, &c1);
           } else {
             const float* pp = a.phi + (bh * L + tgl) * Nr + r0;
-            if (rot0) sincos_wrapped(wrap2pi(pp[0]), &s0, &c0);
-            if (rot1) sincos_wrapped(wrap2pi(pp[1]), &s1, &c1);
+            if (rot0) sincos_wrapped(wrap_fast(pp[0]), &s0, &c0);
+            if (rot1) sincos_wrapped(wrap_fast(pp[1]), &s1, &c1);
           }
-          const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tgl * a.q_st.l;
-          const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tgl * a.k_st.l;
-          const uint32_t uq_lo = *reinterpret_cast<const uint32_t*>(qr + r0);
-          const uint32_t uq_hi = *reinterpret_cast<const uint32_t*>(qr + 64 + r0);
-          const uint32_t uk_lo = *reinterpret_cast<const uint32_t*>(kr + r0);
-          const uint32_t uk_hi = *reinterpret_cast<const uint32_t*>(kr + 64 + r0);
+          const uint32_t col_lo = umma::sw128_off(tt, r0 >> 3) + (r0 & 7) * 2;
+          const uint32_t uq_lo = *reinterpret_cast<const uint32_t*>(sm + kQ + col_lo);
+          const uint32_t uq_hi = *reinterpret_cast<const uint32_t*>(sm + kQ + 16384 + col_lo);
+          const uint32_t uk_lo = *reinterpret_cast<const uint32_t*>(sm + kK + col_lo);
+          const uint32_t uk_hi = *reinterpret_cast<const uint32_t*>(sm + kK + 16384 + col_lo);
           const float ul0 = bf16lo(uq_lo) + qbl.x, ul1 = bf16hi(uq_lo) + qbl.y;
           const float uh0 = bf16lo(uq_hi) + qbh.x, uh1 = bf16hi(uq_hi) + qbh.y;
           const float wl0 = bf16lo(uk_lo) + kbl.x, wl1 = bf16hi(uk_lo) + kbl.y;
@@ -271,9 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
           const float kl0 = wl0 * c0 - wh0 * s0, kh0 = wh0 * c0 + wl0 * s0;
           const float kl1 = wl1 * c1 - wh1 * s1, kh1 = wh1 * c1 + wl1 * s1;
           const float sc = scls[tt];
+          // u.w (pre-rotation) of token tt: the warp's 32 lanes cover all N columns
+          const float uwp = warp_sum(ul0 * wl0 + ul1 * wl1 + uh0 * wh0 + uh1 * wh1);
+          if (lane == 0) reinterpret_cast<float*>(sm + kVd + kScrUw)[tt] = uwp;
           // element (row tt, col k) of a K-major SW128 tile pair: k / 64 picks the
           // 16 KB block, (k % 64) / 8 the 16-byte chunk, k % 8 the bf16 inside it
-          const uint32_t col_lo = umma::sw128_off(tt, r0 >> 3) + (r0 & 7) * 2;
           *reinterpret_cast<uint32_t*>(sm + kQ + col_lo) = umma::pack_bf16x2(ql0, ql1);
           *reinterpret_cast<uint32_t*>(sm + kQ + 16384 + col_lo) = umma::pack_bf16x2(qh0, qh1);
           *reinterpret_cast<uint32_t*>(sm + kK + col_lo) = umma::pack_bf16x2(kl0 * sc, kl1 * sc);
@@ -287,54 +379,34 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
           }
         }
       }
-      // u.w for the diagonal term: each half sums 64 of the N columns of its token
-      {
-        const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tg * a.q_st.l + 64 * half;
-        const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tg * a.k_st.l + 64 * half;
-        const float* qb = a.q_bias + h * kN + 64 * half;
-        const float* kb = a.k_bias + h * kN + 64 * half;
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 uq = *reinterpret_cast<const uint4*>(qr + 8 * j);
-          const uint4 uk = *reinterpret_cast<const uint4*>(kr + 8 * j);
-          const uint32_t qa[4] = {uq.x, uq.y, uq.z, uq.w}, ka[4] = {uk.x, uk.y, uk.z, uk.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = 8 * j + 2 * e;
-            acc += (bf16lo(qa[e]) + qb[n]) * (bf16lo(ka[e]) + kb[n]);
-            acc += (bf16hi(qa[e]) + qb[n + 1]) * (bf16hi(ka[e]) + kb[n + 1]);
-          }
-        }
-        reinterpret_cast<float*>(sm + kVd + kScrUw)[half * 128 + t] = acc;
-      }
+      M3_TC_MARK(1);
       slot_sync(slot);
       float dg;
       {
         const float* uwp = reinterpret_cast<const float*>(sm + kVd + kScrUw);
-        dg = (uwp[t] + uwp[128 + t]) * gam + Dh;
+        dg = uwp[t] * gam + Dh;
       }
       if (RAW && ltid < 64) {
         const float* segtot = reinterpret_cast<const float*>(sm + kVd + kScrSeg);
         float tot = ss->carry[ltid];
         for (int g = 0; g < 8; ++g) tot += segtot[g * 64 + ltid];
-        ss->carry[ltid] = wrap2pi(tot);
+        ss->carry[ltid] = wrap_fast(tot);
       }
       slot_sync(slot);
 
+      M3_TC_MARK(2);
       // ---- phase 3: v and v exp2(A_last - A) tiles (MN-major: row = token) -------------
       uint32_t vreg[16];  // this thread's 32 v values (bf16 pairs), kept for the diagonal term
       {
-        const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)tg * a.v_st.l + 32 * half;
         const float e = exp2f(Alast - A);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const uint4 u = *reinterpret_cast<const uint4*>(vr + 8 * j);
+          const uint4 u = *reinterpret_cast<const uint4*>(sm + kV + umma::sw128_off(t, 4 * half + j));
           vreg[4 * j + 0] = u.x;
           vreg[4 * j + 1] = u.y;
           vreg[4 * j + 2] = u.z;
           vreg[4 * j + 3] = u.w;
-          *reinterpret_cast<uint4*>(sm + kV + umma::sw128_off(t, 4 * half + j)) = u;
+
           uint4 d;
           d.x = umma::pack_bf16x2(bf16lo(u.x) * e, bf16hi(u.x) * e);
           d.y = umma::pack_bf16x2(bf16lo(u.y) * e, bf16hi(u.y) * e);
@@ -348,6 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       slot_sync(slot);
       umma::fence_after_sync();
 
+      M3_TC_MARK(3);
       // ---- phase 4: S, Yi, dSt on the tensor core ----------------------------------------
       if (ltid == 0) {
         constexpr uint32_t id_s = umma::idesc_bf16(128, 128, false, false);
@@ -372,6 +445,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       }
       umma::fence_after_sync();
 
+      // the khat tile is free until the next chunk: stage this thread's z row pieces there
+      if (z) {
+        const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) umma::cp_async16(sK + umma::sw128_off(t, 4 * half + j), zr + 8 * j);
+      }
+      umma::cp_async_commit();
+      M3_TC_MARK(4);
       // ---- phase 5a: state update (St lane n = t, columns 32 half ..) ---------------------
       {
         if (a.chunk_states && c % chunk_sub == 0) {
@@ -412,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int s = sb + 8 * j + e;
-              m[e] = (any && s < t) ? sv[8 * j + e] * exp2f(fminf(A - As[s], 0.f)) : 0.f;
+              m[e] = (any && s < t) ? sv[8 * j + e] * ex2(fminf(A - As[s], 0.f)) : 0.f;
             }
             *reinterpret_cast<uint4*>(sm + kQ + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(m);
           }
@@ -438,6 +519,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
         break;
       }
       umma::fence_after_sync();
+      if (c + 1 < nchunk) {  // the q~ and v tiles are free again
+        prefetch_qv(c + 1);
+        load_scalars(c + 1);
+      } else {
+        umma::cp_async_commit();  // an empty group keeps the wait_group count below exact
+      }
+      M3_TC_MARK(5);
 
       // ---- phase 6: output -----------------------------------------------------------------
       {
@@ -458,16 +546,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
           for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yb + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
         }
         if (z) {
-          const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
+          // the z group was committed before the q~ / v prefetch: wait for all but that one
+          asm volatile("cp.async.wait_group %0;" ::"n"(1) : "memory");
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint4 u = *reinterpret_cast<const uint4*>(zr + 8 * j);
+            const uint4 u = *reinterpret_cast<const uint4*>(sm + kK + umma::sw128_off(t, 4 * half + j));
             const uint32_t zz[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float z0 = bf16lo(zz[e]), z1 = bf16hi(zz[e]);
-              o[8 * j + 2 * e] *= z0 * sigmoidf_(z0);
-              o[8 * j + 2 * e + 1] *= z1 * sigmoidf_(z1);
+              o[8 * j + 2 * e] *= silu_fast(z0);
+              o[8 * j + 2 * e + 1] *= silu_fast(z1);
             }
           }
         }
@@ -475,9 +564,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
 #pragma unroll
         for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(yr + 8 * j) = pack8(o + 8 * j);
       }
+      umma::cp_async_wait_all();  // z reads done and nothing of ours still lands in the khat tile
       umma::fence_before_sync();
       slot_sync(slot);
       umma::fence_after_sync();
+      if (c + 1 < nchunk) prefetch_k(c + 1);
+      umma::fence_before_sync();
+      slot_sync(slot);
+      umma::fence_after_sync();
+      M3_TC_MARK(6);
     }
 
     // ---- final state (kernel_fwd.py:189-201) ---------------------------------------------

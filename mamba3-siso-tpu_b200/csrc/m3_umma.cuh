@@ -119,6 +119,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
   return false;
 }
 
+// ---- cp.async: 16-byte global -> shared copies that do not occupy registers -----------
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // ---- SWIZZLE_128B tile addressing (bf16) ----------------------------------------------
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a tile whose rows
 // are 128 bytes and whose base is 1024-byte aligned.
