@@ -103,8 +103,8 @@ typedef struct M3FwdArgs {
 } M3FwdArgs;
 
 /* Kernel selection for m3_siso_fwd.  AUTO uses the tcgen05 tensor-core kernel where it
- * applies (bf16 I/O, bf16 policy, N = 128, P = 64, chunk % 128 == 0, n_angles <= 64,
- * 16-byte aligned rows) and the generic CUDA-core kernel otherwise. */
+ * applies (bf16 I/O, bf16 policy, N = 128, P = 64, chunk % 128 == 0, n_angles a
+ * multiple of 8 and <= 64, 16-byte aligned rows) and the generic CUDA-core kernel otherwise. */
 enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2 };
 
 int m3_siso_fwd(const M3FwdArgs *args, void *stream);

@@ -28,7 +28,7 @@ static bool fwd_tc_eligible(const M3FwdArgs& a) {
   const M3Dims& d = a.dims;
   if (!(d.state_dim == tc::kN && d.headdim == tc::kP && a.io_dtype == M3_DTYPE_BF16 && a.policy == M3_POLICY_BF16))
     return false;
-  if (d.chunk % tc::kC != 0 || d.seqlen % tc::kC != 0 || d.n_angles > 64) return false;
+  if (d.chunk % tc::kC != 0 || d.seqlen % tc::kC != 0 || d.n_angles > 64 || d.n_angles % 8 != 0) return false;
   // 16-byte vector access to rows of q, k, v, z, y; 8-byte to the bias / angle pairs
   auto rows_ok = [](const void* p, const M3Strides& s, bool bhl) {
     if (!p) return true;
@@ -38,7 +38,8 @@ static bool fwd_tc_eligible(const M3FwdArgs& a) {
       !rows_ok(a.z, a.z_st, true) || !rows_ok(a.y, a.y_st, true))
     return false;
   if (((uintptr_t)a.q_bias & 7u) || ((uintptr_t)a.k_bias & 7u)) return false;
-  if (a.raw && (((uintptr_t)a.angles & 7u) || (a.ang_st.b % 2) || (a.ang_st.l % 2))) return false;
+  if (a.raw && (!al16(a.angles) || (a.ang_st.b % 4) || (a.ang_st.l % 4))) return false;
+  if (!a.raw && !al16(a.phi)) return false;
   if (a.ybar && !al16(a.ybar)) return false;
   return true;
 }
@@ -63,7 +64,7 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   if (a.kernel == M3_KERNEL_TENSORCORE && !tc_ok)
     return set_error(M3_ERR_UNSUPPORTED,
                      "tensor-core forward needs bf16 I/O, bf16 policy, N=128, P=64, chunk % 128 == 0, "
-                     "n_angles <= 64 and 16-byte aligned rows");
+                     "n_angles a multiple of 8 and <= 64, and 16-byte aligned rows");
   if (tc_ok && a.kernel != M3_KERNEL_GENERIC) return run_fwd_tc(a, s);
   const bool mmb = a.policy == M3_POLICY_BF16;
   const bool bf = a.io_dtype == M3_DTYPE_BF16;

@@ -54,12 +54,11 @@ constexpr int kSlotThreads = 256;
 constexpr int kThreads = 2 * kSlotThreads;
 constexpr uint32_t kQ = 0, kK = 32768, kV = 65536, kVd = 81920, kSt = 98304, kSlotBytes = 114688;
 // scratch laid over the vd tile while it is not live
-constexpr uint32_t kScrDt = 0, kScrScl = 512, kScrSeg = 1024, kScrUw = 3072, kScrA = 0;
+constexpr uint32_t kScrDt = 0, kScrScl = 512, kScrUw = 1024, kScrA = 0;  // uw: [8][128] floats
 
 struct SlotSmall {
   uint64_t mbar[2];
   float wtot[4];
-  float carry[64];
 };
 struct CtaSmall {
   SlotSmall slot[2];
@@ -157,7 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
     const int b = seq / H, h = seq % H;
     const size_t bh = (size_t)seq;
     const int t = ltid & 127, half = ltid >> 7;    // token row / state row, column half
-    const int rp = lane, sg = lwarp;               // angle pair (2 rp, 2 rp + 1), 16-token segment
     const uint32_t lane_base = (uint32_t)(32 * (lwarp & 3)) << 16;
     const __nv_bfloat16* q = (const __nv_bfloat16*)a.q;
     const __nv_bfloat16* k = (const __nv_bfloat16*)a.k;
@@ -171,14 +169,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
     const uint32_t sVd = umma::smem_u32(sm + kVd), sSt = umma::smem_u32(sm + kSt);
     bool ok = true;
 
-    // per-thread bias pairs for the rotation role: columns 2rp, 2rp+1 (lo) and +64 (hi)
-    const float2 qbl = *reinterpret_cast<const float2*>(a.q_bias + h * kN + 2 * rp);
-    const float2 qbh = *reinterpret_cast<const float2*>(a.q_bias + h * kN + 64 + 2 * rp);
-    const float2 kbl = *reinterpret_cast<const float2*>(a.k_bias + h * kN + 2 * rp);
-    const float2 kbh = *reinterpret_cast<const float2*>(a.k_bias + h * kN + 64 + 2 * rp);
-
     // ---- initial state: registers hold St[n = t][p = 32 half + i] (fp32) ------------
     float st[32];
+    float carry8[8];
     {
       float coef = 0.f;
       if (a.seed_ssm) {
@@ -198,7 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(st + 8 * j);
-      if (RAW && ltid < 64) ss->carry[ltid] = (a.seed_phi && ltid < Nr) ? a.seed_phi[bh * Nr + ltid] : 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)  // angle carry of this warp's rotary group (raw boundary)
+        carry8[r] = (RAW && a.seed_phi && 8 * lwarp + r < Nr) ? a.seed_phi[bh * Nr + 8 * lwarp + r] : 0.f;
     }
     slot_sync(slot);
 
@@ -295,102 +290,113 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       const float Alast = ss->wtot[0] + ss->wtot[1] + ss->wtot[2] + ss->wtot[3];
       M3_TC_MARK(0);
 
-      // ---- phase 2: cumulative angles, rotation ---------------------------------------
+      // ---- phase 2: cumulative angles and rotation ---------------------------------------
+      // Warp g owns rotary pairs (8g .. 8g+7, 64+8g .. 64+8g+7): one 16-byte swizzle chunk
+      // of each q / k half-row.  Lane l owns tokens l + 32 i; the prefix over tokens is a
+      // warp scan per angle and 32-token block, and the carry across chunks stays in
+      // registers (the same value in every lane of the warp).
       {
         const float* dts = reinterpret_cast<const float*>(sm + kVd + kScrDt);
         const float* scls = reinterpret_cast<const float*>(sm + kVd + kScrScl);
-        float* segtot = reinterpret_cast<float*>(sm + kVd + kScrSeg);  // [8][64]
-        const int r0 = 2 * rp;
-        const bool rot0 = r0 < Nr, rot1 = r0 + 1 < Nr;
-        float th0[16], th1[16];
-        float off0 = 0.f, off1 = 0.f;
-        if (RAW) {
-          float s0 = 0.f, s1 = 0.f;
-          // every load first (in-row column indices, so always in bounds), then the math
-          const int c0i = min(r0, Nr - 1), c1i = min(r0 + 1, Nr - 1);
-          const float* abase = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + sg * 16) * a.ang_st.l;
+        float* uws = reinterpret_cast<float*>(sm + kVd + kScrUw);  // [8 groups][128 tokens]
+        const int g = lwarp;
+        const bool grot = 8 * g < Nr;  // Nr % 8 == 0: a group rotates entirely or not at all
+        const float* qbp = a.q_bias + h * kN + 8 * g;
+        const float* kbp = a.k_bias + h * kN + 8 * g;
+        float off[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            th0[i] = abase[(size_t)i * a.ang_st.l + c0i];
-            th1[i] = abase[(size_t)i * a.ang_st.l + c1i];
-          }
+        for (int r = 0; r < 8; ++r) off[r] = carry8[r];
+#pragma unroll 1
+        for (int i = 0; i < 4; ++i) {
+          const int tt = lane + 32 * i, tgl = t0 + tt;
+          float ph[8];
+          if (grot) {
+            const float* pp = RAW ? a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g
+                                  : a.phi + (bh * L + tgl) * Nr + 8 * g;
+            const float4 lo = *reinterpret_cast<const float4*>(pp);
+            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+            ph[0] = lo.x; ph[1] = lo.y; ph[2] = lo.z; ph[3] = lo.w;
+            ph[4] = hi.x; ph[5] = hi.y; ph[6] = hi.z; ph[7] = hi.w;
+            if (RAW) {
+              const float w = kPi * dts[tt];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float w = kPi * dts[sg * 16 + i];
-            th0[i] = rot0 ? tanh_acc(th0[i]) * w : 0.f;
-            th1[i] = rot1 ? tanh_acc(th1[i]) * w : 0.f;
-            s0 += th0[i];
-            s1 += th1[i];
+              for (int r = 0; r < 8; ++r) {
+                const float th = tanh_acc(ph[r]) * w;
+                const float incl = warp_inclusive_scan(th);
+                ph[r] = off[r] + incl;
+                off[r] += __shfl_sync(0xffffffffu, incl, 31);
+              }
+            }
           }
-          segtot[sg * 64 + r0] = s0;
-          segtot[sg * 64 + r0 + 1] = s1;
-          slot_sync(slot);
-          M3_TC_MARK(7);
-          off0 = rot0 ? ss->carry[r0] : 0.f;
-          off1 = rot1 ? ss->carry[r0 + 1] : 0.f;
-          for (int g = 0; g < sg; ++g) {
-            off0 += segtot[g * 64 + r0];
-            off1 += segtot[g * 64 + r0 + 1];
+          float cs[8], sn[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            cs[r] = 1.f;
+            sn[r] = 0.f;
+            if (grot) sincos_wrapped(wrap_fast(ph[r]), &sn[r], &cs[r]);
           }
-        }
-#pragma unroll 4
-        for (int i = 0; i < 16; ++i) {
-          const int tt = sg * 16 + i, tgl = t0 + tt;
-          float c0 = 1.f, s0 = 0.f, c1 = 1.f, s1 = 0.f;
-          if (RAW) {
-            off0 += th0[i];
-            off1 += th1[i];
-            if (rot0) sincos_wrapped(wrap_fast(off0), &s0, &c0);
-            if (rot1) sincos_wrapped(wrap_fast(off1), &s1, &c1);
-          } else {
-            const float* pp = a.phi + (bh * L + tgl) * Nr + r0;
-            if (rot0) sincos_wrapped(wrap_fast(pp[0]), &s0, &c0);
-            if (rot1) sincos_wrapped(wrap_fast(pp[1]), &s1, &c1);
-          }
-          const uint32_t col_lo = umma::sw128_off(tt, r0 >> 3) + (r0 & 7) * 2;
-          const uint32_t uq_lo = *reinterpret_cast<const uint32_t*>(sm + kQ + col_lo);
-          const uint32_t uq_hi = *reinterpret_cast<const uint32_t*>(sm + kQ + 16384 + col_lo);
-          const uint32_t uk_lo = *reinterpret_cast<const uint32_t*>(sm + kK + col_lo);
-          const uint32_t uk_hi = *reinterpret_cast<const uint32_t*>(sm + kK + 16384 + col_lo);
-          const float ul0 = bf16lo(uq_lo) + qbl.x, ul1 = bf16hi(uq_lo) + qbl.y;
-          const float uh0 = bf16lo(uq_hi) + qbh.x, uh1 = bf16hi(uq_hi) + qbh.y;
-          const float wl0 = bf16lo(uk_lo) + kbl.x, wl1 = bf16hi(uk_lo) + kbl.y;
-          const float wh0 = bf16lo(uk_hi) + kbh.x, wh1 = bf16hi(uk_hi) + kbh.y;
-          const float ql0 = ul0 * c0 - uh0 * s0, qh0 = uh0 * c0 + ul0 * s0;
-          const float ql1 = ul1 * c1 - uh1 * s1, qh1 = uh1 * c1 + ul1 * s1;
-          const float kl0 = wl0 * c0 - wh0 * s0, kh0 = wh0 * c0 + wl0 * s0;
-          const float kl1 = wl1 * c1 - wh1 * s1, kh1 = wh1 * c1 + wl1 * s1;
+          const uint32_t soff = umma::sw128_off(tt, g);
+          const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
+          const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+          const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
+          const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
+          const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
+          const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
           const float sc = scls[tt];
-          // u.w (pre-rotation) of token tt: the warp's 32 lanes cover all N columns
-          const float uwp = warp_sum(ul0 * wl0 + ul1 * wl1 + uh0 * wh0 + uh1 * wh1);
-          if (lane == 0) reinterpret_cast<float*>(sm + kVd + kScrUw)[tt] = uwp;
-          // element (row tt, col k) of a K-major SW128 tile pair: k / 64 picks the
-          // 16 KB block, (k % 64) / 8 the 16-byte chunk, k % 8 the bf16 inside it
-          *reinterpret_cast<uint32_t*>(sm + kQ + col_lo) = umma::pack_bf16x2(ql0, ql1);
-          *reinterpret_cast<uint32_t*>(sm + kQ + 16384 + col_lo) = umma::pack_bf16x2(qh0, qh1);
-          *reinterpret_cast<uint32_t*>(sm + kK + col_lo) = umma::pack_bf16x2(kl0 * sc, kl1 * sc);
-          *reinterpret_cast<uint32_t*>(sm + kK + 16384 + col_lo) = umma::pack_bf16x2(kh0 * sc, kh1 * sc);
-          if (tgl == L - 1) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
-            float* fk = a.final_k + bh * kN;
-            fk[r0] = kl0;
-            fk[r0 + 1] = kl1;
-            fk[64 + r0] = kh0;
-            fk[64 + r0 + 1] = kh1;
+          float oq_lo[8], oq_hi[8], ok_lo[8], ok_hi[8];
+          float uw = 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 bql = __ldg(reinterpret_cast<const float2*>(qbp + 2 * e));
+            const float2 bqh = __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
+            const float2 bkl = __ldg(reinterpret_cast<const float2*>(kbp + 2 * e));
+            const float2 bkh = __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
+            const float ulo[2] = {bf16lo(ql[e]) + bql.x, bf16hi(ql[e]) + bql.y};
+            const float uhi[2] = {bf16lo(qh[e]) + bqh.x, bf16hi(qh[e]) + bqh.y};
+            const float wlo[2] = {bf16lo(kl[e]) + bkl.x, bf16hi(kl[e]) + bkl.y};
+            const float whi[2] = {bf16lo(kh[e]) + bkh.x, bf16hi(kh[e]) + bkh.y};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int r = 2 * e + u;
+              uw += ulo[u] * wlo[u] + uhi[u] * whi[u];
+              oq_lo[r] = ulo[u] * cs[r] - uhi[u] * sn[r];
+              oq_hi[r] = uhi[u] * cs[r] + ulo[u] * sn[r];
+              ok_lo[r] = wlo[u] * cs[r] - whi[u] * sn[r];
+              ok_hi[r] = whi[u] * cs[r] + wlo[u] * sn[r];
+            }
           }
+          if (tgl == L - 1) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
+            float* fk = a.final_k + bh * kN + 8 * g;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+              fk[r] = ok_lo[r];
+              fk[64 + r] = ok_hi[r];
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            ok_lo[r] *= sc;
+            ok_hi[r] *= sc;
+          }
+          *reinterpret_cast<uint4*>(sm + kQ + soff) = pack8(oq_lo);
+          *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = pack8(oq_hi);
+          *reinterpret_cast<uint4*>(sm + kK + soff) = pack8(ok_lo);
+          *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = pack8(ok_hi);
+          uws[g * 128 + tt] = uw;
         }
+        if (RAW)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) carry8[r] = wrap_fast(off[r]);
       }
       M3_TC_MARK(1);
       slot_sync(slot);
       float dg;
       {
-        const float* uwp = reinterpret_cast<const float*>(sm + kVd + kScrUw);
-        dg = uwp[t] * gam + Dh;
-      }
-      if (RAW && ltid < 64) {
-        const float* segtot = reinterpret_cast<const float*>(sm + kVd + kScrSeg);
-        float tot = ss->carry[ltid];
-        for (int g = 0; g < 8; ++g) tot += segtot[g * 64 + ltid];
-        ss->carry[ltid] = wrap_fast(tot);
+        const float* uws = reinterpret_cast<const float*>(sm + kVd + kScrUw);
+        float uw = 0.f;
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) uw += uws[gg * 128 + t];
+        dg = uw * gam + Dh;
       }
       slot_sync(slot);
 
@@ -493,7 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const int s = sb + 8 * j + e;
-              m[e] = (any && s < t) ? sv[8 * j + e] * ex2(fminf(A - As[s], 0.f)) : 0.f;
+              float val = 0.f;
+              if (any && s < t) val = sv[8 * j + e] * ex2(fminf(A - As[s], 0.f));
+              m[e] = val;
             }
             *reinterpret_cast<uint4*>(sm + kQ + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(m);
           }
@@ -582,8 +590,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(L - 1) * a.v_st.l;
       a.final_v[bh * kP + ltid] = __bfloat162float(vr[ltid]);
     }
-    if (a.final_phi && ltid < Nr)
-      a.final_phi[bh * Nr + ltid] = RAW ? ss->carry[ltid] : a.phi[(bh * L + L - 1) * Nr + ltid];
+    if (a.final_phi) {
+      if (RAW) {
+        if (lane == 0 && 8 * lwarp < Nr)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) a.final_phi[bh * Nr + 8 * lwarp + r] = carry8[r];
+      } else if (ltid < Nr) {
+        a.final_phi[bh * Nr + ltid] = a.phi[(bh * L + L - 1) * Nr + ltid];
+      }
+    }
   }
   umma::fence_before_sync();
   __syncthreads();
