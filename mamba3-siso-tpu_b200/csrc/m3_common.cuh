@@ -38,6 +38,32 @@ __device__ __forceinline__ float heavy_tail(float x) { return fmaxf(x, 0.f) + 1.
 // phi - 2 pi floor(phi / 2 pi)  (reference.py:156)
 __device__ __forceinline__ float wrap2pi(float x) { return x - kTwoPi * floorf(x / kTwoPi); }
 
+// sin / cos of an angle in [0, 2 pi) through the SFU (accurate on [-pi, pi]).
+__device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
+  if (x >= kPi) x -= kTwoPi;
+  __sincosf(x, s, c);
+}
+
+// 2^x on the SFU (relative error ~2^-22; flushes subnormal results to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// phi - 2 pi floor(phi / 2 pi) with a reciprocal multiply instead of a division.
+__device__ __forceinline__ float wrap_fast(float x) {
+  return x - kTwoPi * floorf(x * 0.15915494309189535f);
+}
+
+// tanh from exp2 and a correctly rounded reciprocal: |error| ~ 1e-7 absolute and
+// unbiased, so the cumulative angle does not drift (tanh.approx's 2^-11 would).
+__device__ __forceinline__ float tanh_acc(float x) {
+  const float e = ex2(2.f * kLog2e * fminf(fabsf(x), 15.f));
+  const float t = 1.f - 2.f * __frcp_rn(e + 1.f);
+  return copysignf(t, x);
+}
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

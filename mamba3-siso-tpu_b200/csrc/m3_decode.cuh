@@ -26,11 +26,13 @@ struct DecVec {
 
 template <int V> struct F4 { float x[V]; };
 
+// The state is read once and written once per step: stream it past L1 / L2 residency
+// (evict-first loads, streaming stores).
 template <int V>
 __device__ __forceinline__ F4<V> ldv(const float* p) {
   F4<V> r;
   if constexpr (V == 4) {
-    float4 t = *reinterpret_cast<const float4*>(p);
+    float4 t = __ldcs(reinterpret_cast<const float4*>(p));
     r.x[0] = t.x; r.x[1] = t.y; r.x[2] = t.z; r.x[3] = t.w;
   } else if constexpr (V == 2) {
     float2 t = *reinterpret_cast<const float2*>(p);
@@ -45,7 +47,7 @@ __device__ __forceinline__ F4<V> ldv(const float* p) {
 template <int V>
 __device__ __forceinline__ void stv(float* p, const F4<V>& r) {
   if constexpr (V == 4) {
-    *reinterpret_cast<float4*>(p) = make_float4(r.x[0], r.x[1], r.x[2], r.x[3]);
+    __stcs(reinterpret_cast<float4*>(p), make_float4(r.x[0], r.x[1], r.x[2], r.x[3]));
   } else if constexpr (V == 2) {
     *reinterpret_cast<float2*>(p) = make_float2(r.x[0], r.x[1]);
   } else {
@@ -55,7 +57,7 @@ __device__ __forceinline__ void stv(float* p, const F4<V>& r) {
 }
 
 template <int N, int P, typename T, bool MMB>
-__global__ void __launch_bounds__(kDecThreads) decode_kernel(const M3DecodeArgs a) {
+__global__ void __launch_bounds__(kDecThreads, 4) decode_kernel(const M3DecodeArgs a) {
   constexpr int V = DecVec<N>::V, LANES = DecVec<N>::LANES, H2 = N / 2;
   constexpr int NW = kDecThreads / 32;
   constexpr int RPW = (P + NW - 1) / NW;  // rows per warp
@@ -106,13 +108,13 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const M3DecodeArgs 
     const float w = ld(k + n) + a.k_bias[h * N + n];
     float qv = u, kv = w;
     if (j < Nr) {
-      const float ph = wrap2pi(a.phi[bh * Nr + j] + tanhf(a.angles[(size_t)b * a.ang_stride_b + j]) * kPi * dt);
+      const float ph = wrap_fast(a.phi[bh * Nr + j] + tanh_acc(a.angles[(size_t)b * a.ang_stride_b + j]) * kPi * dt);
       phi_new[i] = ph;
       const int m = n < H2 ? n + H2 : n - H2;  // the pair partner
       const float um = ld(q + m) + a.q_bias[h * N + m];
       const float wm = ld(k + m) + a.k_bias[h * N + m];
       float sn, cs;
-      sincosf(ph, &sn, &cs);
+      sincos_wrapped(ph, &sn, &cs);
       // x cos + rot_half(x) sin, rot_half = [-hi, lo]  (layout.py:375-398)
       const float sgn = n < H2 ? -1.f : 1.f;
       qv = u * cs + sgn * um * sn;

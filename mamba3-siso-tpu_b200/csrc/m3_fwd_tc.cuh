@@ -88,32 +88,6 @@ __device__ __forceinline__ bool slot_any(int slot, bool pred) {
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 
-// sin / cos of an angle in [0, 2 pi) through the SFU (accurate on [-pi, pi]).
-__device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
-  if (x >= kPi) x -= kTwoPi;
-  __sincosf(x, s, c);
-}
-
-// 2^x on the SFU (relative error ~2^-22; flushes subnormal results to zero).
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// phi - 2 pi floor(phi / 2 pi) with a reciprocal multiply instead of a division.
-__device__ __forceinline__ float wrap_fast(float x) {
-  return x - kTwoPi * floorf(x * 0.15915494309189535f);
-}
-
-// tanh from exp2 and a correctly rounded reciprocal: |error| ~ 1e-7 absolute and
-// unbiased, so the cumulative angle does not drift (tanh.approx's 2^-11 would).
-__device__ __forceinline__ float tanh_acc(float x) {
-  const float e = ex2(2.f * kLog2e * fminf(fabsf(x), 15.f));
-  const float t = 1.f - 2.f * __frcp_rn(e + 1.f);
-  return copysignf(t, x);
-}
-
 // z sigmoid(z) for the output gate (bf16 output: the SFU exp and reciprocal suffice).
 __device__ __forceinline__ float silu_fast(float z) { return z * __frcp_rn(1.f + __expf(-z)); }
 
