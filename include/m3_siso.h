@@ -102,9 +102,10 @@ typedef struct M3FwdArgs {
   int32_t kernel;                       /* M3_KERNEL_*: 0 = pick automatically */
 } M3FwdArgs;
 
-/* Kernel selection for m3_siso_fwd.  AUTO uses the tcgen05 tensor-core kernel where it
+/* Kernel selection for m3_siso_fwd / m3_siso_bwd.  AUTO uses the tcgen05 tensor-core kernel where it
  * applies (bf16 I/O, bf16 policy, N = 128, P = 64, chunk % 128 == 0, n_angles a
- * multiple of 8 and <= 64, 16-byte aligned rows) and the generic CUDA-core kernel otherwise. */
+ * multiple of 8 and <= 64, 16-byte aligned rows; for the backward also the raw boundary)
+ * and the generic CUDA-core kernel otherwise. */
 enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2 };
 
 int m3_siso_fwd(const M3FwdArgs *args, void *stream);
@@ -149,6 +150,8 @@ typedef struct M3BwdArgs {
 
   void *workspace;
   size_t workspace_bytes;
+
+  int32_t kernel;                         /* M3_KERNEL_*: 0 = pick automatically */
 } M3BwdArgs;
 
 size_t m3_siso_bwd_workspace_size(const M3Dims *dims);

@@ -5,7 +5,9 @@
 namespace m3 {
 
 size_t bwd_workspace_bytes(const M3Dims& d) {
-  return sizeof(float) * (bwd_ws_state_floats(d) + bwd_ws_phi_floats(d)) + 256;
+  const size_t simt = sizeof(float) * (bwd_ws_state_floats(d) + bwd_ws_phi_floats(d)) + 256;
+  const size_t tcw = (d.seqlen % 128 == 0) ? bwd_tc_workspace_bytes(d) : 0;
+  return simt > tcw ? simt : tcw;
 }
 
 template <int N, int P, typename T, bool MMB>

@@ -1,0 +1,755 @@
+// Tensor-core (tcgen05 / TMEM) backward for the production shape: bf16 I/O and bf16
+// matmul operands, N = 128, P = 64, 128-token chunks, raw (fused-preprocess) boundary.
+//
+// The chunk-start states are recomputed first by the forward kernel's states-only mode
+// (bf16 tiles in the layout used below, plus the rotary-angle carries); nothing is read
+// from the forward's residuals.  Then one CTA (256 threads) per (b, h) walks the chunks in
+// reverse with the adjoint G of the chunk's end state in registers (fp32), per chunk
+// (kernel_bwd.py:10-34, 103-355; A_t the prefix of adt log2 e inside the chunk):
+//
+//   round 1  Wm  = q~ khat^T         dM = g v^T            Yi = q~ S^T
+//   CUDA     one decay mask exp2(min(A_i - A_j, 0)), strict lower triangle, for both
+//   round 2  Ya  = Wm v              dv_a = Wm^T g         dv_b = khat G^T
+//            dq~ = dM khat + (e^A g) S                      dkhat = dM^T q~ + vd G
+//   CUDA     ybar -> dz, dv, rotation pullback (fp32, recomputed angles), head-summed
+//            dq / dk, bias and angle adjoints, the autodiff of the preprocessing
+//   round 3  dG^T = q~^T (e^A g);    G <- exp2(A_last) G + dG
+//
+// with vd = v exp2(A_last - A) and e^A g folded into bf16 operands.  The A_last term of
+// dadt is sum(G o S_next): every occurrence of A_last scales the chunk's end state
+// S_next = exp2(A_last) S + vd^T khat, so its adjoint is exactly that inner product.
+#pragma once
+
+#include "m3_chunk_common.cuh"
+#include "m3_fwd_tc.cuh"
+#include "m3_umma.cuh"
+
+namespace m3 {
+namespace tcb {
+
+using tc::bf16hi;
+using tc::bf16lo;
+using tc::pack8;
+
+constexpr int kN = 128, kP = 64, kC = 128, kThreads = 256;
+// tile offsets (bytes); everything from kK on is free once round 2 has completed
+constexpr uint32_t kQ = 0, kGe = 32768, kSt = 49152, kGt = 65536, kK = 81920, kWm = 114688, kDM = 147456,
+                   kV = 180224, kVd = 196608, kG = 212992, kTiles = 229376;
+// scratch inside tiles while they are not live
+constexpr uint32_t kScrDt = kWm, kScrScl = kWm + 512, kScrUw = kWm + 1024, kScrQkd = kWm + 5120;   // prep
+constexpr uint32_t kScrPart = kGt, kScrDtb = kGt + 2048, kScrTh = kGt + 2560;                     // epilogue
+constexpr uint32_t kDu = kK, kDw = kDM;  // fp32 [128][128] each, column index XOR-swizzled by row
+
+struct Small {
+  uint64_t mbar[3];
+  uint32_t tmem;
+  float alast;
+  float wtot[4];
+  float red[8];
+  float A[128];
+};
+constexpr size_t kSmemBytes = kTiles + 1024 + 1024;  // tiles + Small (<= 1 KB) + alignment slack
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// Sum over the CTA (every thread gets the total).
+__device__ __forceinline__ float cta_sum(float x, Small* sm_) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  x = warp_sum(x);
+  __syncthreads();
+  if (lane == 0) sm_->red[warp] = x;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += sm_->red[w];
+  __syncthreads();
+  return t;
+}
+
+// Inclusive suffix scan over the 32 lanes of a warp (lane l gets sum of lanes >= l).
+__device__ __forceinline__ float warp_suffix_scan(float x) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x += y;
+  }
+  return x;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_tc_kernel(const M3BwdArgs a, const uint8_t* __restrict__ tiles, const float* __restrict__ phis,
+                  float* __restrict__ scratch) {
+  extern __shared__ uint8_t smraw[];
+  uint8_t* sm = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
+  Small* ss = reinterpret_cast<Small*>(sm + kTiles);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t = tid & 127, half = tid >> 7;  // token / state row and column half
+  const int H = a.dims.nheads, L = a.dims.seqlen, Nr = a.dims.n_angles;
+  const int seq = blockIdx.x, b = seq / H, h = seq % H;
+  const size_t bh = (size_t)seq;
+  const int nchunk = L / kC;
+  const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+  const __nv_bfloat16* q = (const __nv_bfloat16*)a.q;
+  const __nv_bfloat16* k = (const __nv_bfloat16*)a.k;
+  const __nv_bfloat16* v = (const __nv_bfloat16*)a.v;
+  const __nv_bfloat16* z = (const __nv_bfloat16*)a.z;
+  const __nv_bfloat16* dy = (const __nv_bfloat16*)a.dy;
+  const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
+  const float dtb = a.dt_bias[h];
+  float* phs = scratch + (size_t)blockIdx.x * (kC * 64);  // [t][64]: phi, then dphi
+
+  if (warp == 0) umma::tmem_alloc(&ss->tmem, 512);
+  if (tid == 0) {
+    for (int i = 0; i < 3; ++i) umma::mbar_init(&ss->mbar[i], 1);
+    umma::fence_mbar_init();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tm = ss->tmem;
+  const uint32_t aQ = umma::smem_u32(sm + kQ), aGe = umma::smem_u32(sm + kGe), aSt = umma::smem_u32(sm + kSt);
+  const uint32_t aGt = umma::smem_u32(sm + kGt), aK = umma::smem_u32(sm + kK), aWm = umma::smem_u32(sm + kWm);
+  const uint32_t aDM = umma::smem_u32(sm + kDM), aV = umma::smem_u32(sm + kV), aVd = umma::smem_u32(sm + kVd);
+  const uint32_t aG = umma::smem_u32(sm + kG);
+  bool ok = true;
+
+  // ---- adjoint of the final state: G^T[n = t][p = 32 half + i] (fp32, registers) ------
+  float G[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    G[i] = a.dfinal_ssm ? a.dfinal_ssm[(bh * kP + 32 * half + i) * kN + t] : 0.f;
+  float dcarry8[8];  // adjoint of this warp's rotary-angle carry
+#pragma unroll
+  for (int r = 0; r < 8; ++r) dcarry8[r] = (a.dfinal_phi && 8 * warp + r < Nr) ? a.dfinal_phi[bh * Nr + 8 * warp + r] : 0.f;
+  {
+    // A_last term of the last chunk: sum(G o S_final); S_final is tile `nchunk`
+    const uint8_t* sf = tiles + (bh * (nchunk + 1) + nchunk) * 16384u;
+    float part = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 u = *reinterpret_cast<const uint4*>(sf + umma::sw128_off(t, 4 * half + j));
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) part += G[8 * j + 2 * e] * bf16lo(w4[e]) + G[8 * j + 2 * e + 1] * bf16hi(w4[e]);
+    }
+    const float tot = cta_sum(part, ss);
+    if (tid == 0) ss->alast = tot;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(sm + kGt + umma::sw128_off(t, 4 * half + j)) = pack8(G + 8 * j);
+  }
+  float bias_acc = 0.f, dD_acc = 0.f, ddtb_acc = 0.f;
+  __syncthreads();
+
+  for (int c = nchunk - 1; c >= 0 && ok; --c) {
+    const int t0 = c * kC, tg = t0 + t;
+    const float alast = ss->alast;
+    // ---- P0: raw tiles (cp.async), per-token scalars, g and e^A g -------------------------
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 4, c16 = i & 15;
+      const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
+      umma::cp_async16(aQ + dst, q + (size_t)b * a.q_st.b + (size_t)(t0 + row) * a.q_st.l + c16 * 8);
+      umma::cp_async16(aK + dst, k + (size_t)b * a.k_st.b + (size_t)(t0 + row) * a.k_st.l + c16 * 8);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 3, c8 = i & 7;
+      umma::cp_async16(aV + umma::sw128_off(row, c8),
+                       v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(t0 + row) * a.v_st.l + c8 * 8);
+      umma::cp_async16(aSt + 16u * i, tiles + (bh * (nchunk + 1) + c) * 16384u + 16u * i);
+    }
+    umma::cp_async_commit();
+    const size_t ro = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
+    const float dt = softplusf(a.dt_raw[ro] + dtb);
+    const float lam = sigmoidf_(a.trap_raw[ro]);
+    const float ar = a.a_raw[ro];
+    const float av = fminf(-heavy_tail(ar), -a.a_floor);
+    float dtn = __shfl_down_sync(0xffffffffu, dt, 1), lamn = __shfl_down_sync(0xffffffffu, lam, 1);
+    if (lane == 31) {
+      dtn = tg + 1 < L ? softplusf(a.dt_raw[ro + a.raw_st.l] + dtb) : 0.f;
+      lamn = tg + 1 < L ? sigmoidf_(a.trap_raw[ro + a.raw_st.l]) : 0.f;
+    }
+    const float gam = dt * lam, scl = gam + dtn * (1.f - lamn);
+    const float incl = warp_inclusive_scan(av * dt * kLog2e);
+    if (half == 0 && lane == 31) ss->wtot[warp & 3] = incl;
+    if (half == 0) {
+      reinterpret_cast<float*>(sm + kScrDt)[t] = dt;
+      reinterpret_cast<float*>(sm + kScrScl)[t] = scl;
+    }
+    __syncthreads();
+    float A = incl;
+    for (int w = 0; w < (warp & 3); ++w) A += ss->wtot[w];
+    const float Alast = ss->wtot[0] + ss->wtot[1] + ss->wtot[2] + ss->wtot[3];
+    const float eA = exp2f(A), erev = exp2f(Alast - A);
+    if (half == 0) ss->A[t] = A;
+    // g = dy silu(z) for this thread's 32 columns; bf16 g and e^A g tiles (rows = token)
+    float gv[32];
+    {
+      const __nv_bfloat16* dyr = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tg * a.dy_st.l + 32 * half;
+      const __nv_bfloat16* zr = z ? z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half
+                                  : nullptr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(dyr + 8 * j);
+        const uint32_t d4[4] = {u.x, u.y, u.z, u.w};
+        uint32_t z4[4] = {0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u};
+        if (zr) {
+          const uint4 w = *reinterpret_cast<const uint4*>(zr + 8 * j);
+          z4[0] = w.x; z4[1] = w.y; z4[2] = w.z; z4[3] = w.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float g0 = bf16lo(d4[e]), g1 = bf16hi(d4[e]);
+          if (zr) {
+            const float z0 = bf16lo(z4[e]), z1 = bf16hi(z4[e]);
+            g0 *= z0 * sigmoidf_(z0);
+            g1 *= z1 * sigmoidf_(z1);
+          }
+          gv[8 * j + 2 * e] = g0;
+          gv[8 * j + 2 * e + 1] = g1;
+        }
+      }
+      float ge[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ge[i] = gv[i] * eA;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint4*>(sm + kG + umma::sw128_off(t, 4 * half + j)) = pack8(gv + 8 * j);
+        *reinterpret_cast<uint4*>(sm + kGe + umma::sw128_off(t, 4 * half + j)) = pack8(ge + 8 * j);
+      }
+    }
+    umma::cp_async_wait_all();
+    __syncthreads();
+
+    // ---- P1: cumulative angles (from the recorded carry) and rotation; phi to scratch ----
+    {
+      const float* dts = reinterpret_cast<const float*>(sm + kScrDt);
+      const float* scls = reinterpret_cast<const float*>(sm + kScrScl);
+      float* uws = reinterpret_cast<float*>(sm + kScrUw);
+      const int g = warp;
+      const bool grot = 8 * g < Nr;
+      const float* qbp = a.q_bias + h * kN + 8 * g;
+      const float* kbp = a.k_bias + h * kN + 8 * g;
+      float off[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) off[r] = grot ? phis[(bh * nchunk + c) * Nr + 8 * g + r] : 0.f;
+#pragma unroll 1
+      for (int i = 0; i < 4; ++i) {
+        const int tt = lane + 32 * i, tgl = t0 + tt;
+        float ph[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (grot) {
+          const float* pp = a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g;
+          const float4 lo = *reinterpret_cast<const float4*>(pp);
+          const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+          const float an[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+          const float w = kPi * dts[tt];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float inc = warp_inclusive_scan(tanh_acc(an[r]) * w);
+            ph[r] = off[r] + inc;
+            off[r] += __shfl_sync(0xffffffffu, inc, 31);
+          }
+          float* pw = phs + (size_t)tt * 64 + 8 * g;
+          *reinterpret_cast<float4*>(pw) = make_float4(ph[0], ph[1], ph[2], ph[3]);
+          *reinterpret_cast<float4*>(pw + 4) = make_float4(ph[4], ph[5], ph[6], ph[7]);
+        }
+        float cs[8], sn[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          cs[r] = 1.f;
+          sn[r] = 0.f;
+          if (grot) sincos_wrapped(wrap_fast(ph[r]), &sn[r], &cs[r]);
+        }
+        const uint32_t soff = umma::sw128_off(tt, g);
+        const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
+        const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+        const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
+        const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
+        const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
+        const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
+        const float sc = scls[tt];
+        float oq_lo[8], oq_hi[8], ok_lo[8], ok_hi[8];
+        float uw = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 bql = __ldg(reinterpret_cast<const float2*>(qbp + 2 * e));
+          const float2 bqh = __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
+          const float2 bkl = __ldg(reinterpret_cast<const float2*>(kbp + 2 * e));
+          const float2 bkh = __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
+          const float ulo[2] = {bf16lo(ql[e]) + bql.x, bf16hi(ql[e]) + bql.y};
+          const float uhi[2] = {bf16lo(qh[e]) + bqh.x, bf16hi(qh[e]) + bqh.y};
+          const float wlo[2] = {bf16lo(kl[e]) + bkl.x, bf16hi(kl[e]) + bkl.y};
+          const float whi[2] = {bf16lo(kh[e]) + bkh.x, bf16hi(kh[e]) + bkh.y};
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int r = 2 * e + u;
+            uw += ulo[u] * wlo[u] + uhi[u] * whi[u];
+            oq_lo[r] = ulo[u] * cs[r] - uhi[u] * sn[r];
+            oq_hi[r] = uhi[u] * cs[r] + ulo[u] * sn[r];
+            ok_lo[r] = (wlo[u] * cs[r] - whi[u] * sn[r]) * sc;
+            ok_hi[r] = (whi[u] * cs[r] + wlo[u] * sn[r]) * sc;
+          }
+        }
+        *reinterpret_cast<uint4*>(sm + kQ + soff) = pack8(oq_lo);
+        *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = pack8(oq_hi);
+        *reinterpret_cast<uint4*>(sm + kK + soff) = pack8(ok_lo);
+        *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = pack8(ok_hi);
+        uws[g * 128 + tt] = uw;
+      }
+    }
+    // ---- P2: dqk_diag = g.v (halves), v exp2(A_last - A) tile -------------------------
+    uint32_t vreg[16];
+    {
+      float part = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + kV + umma::sw128_off(t, 4 * half + j));
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        float d[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          vreg[4 * j + e] = w4[e];
+          const float v0 = bf16lo(w4[e]), v1 = bf16hi(w4[e]);
+          part += gv[8 * j + 2 * e] * v0 + gv[8 * j + 2 * e + 1] * v1;
+          d[2 * e] = v0 * erev;
+          d[2 * e + 1] = v1 * erev;
+        }
+        *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + j)) = pack8(d);
+      }
+      reinterpret_cast<float*>(sm + kScrQkd)[half * 128 + t] = part;
+    }
+    umma::fence_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    float uwt = 0.f;
+    {
+      const float* uws = reinterpret_cast<const float*>(sm + kScrUw);
+#pragma unroll
+      for (int gg = 0; gg < 8; ++gg) uwt += uws[gg * 128 + t];
+    }
+    const float dg = uwt * gam + Dh;
+    const float qkd = reinterpret_cast<const float*>(sm + kScrQkd)[t] + reinterpret_cast<const float*>(sm + kScrQkd)[128 + t];
+
+    // ---- round 1: Wm, dM, Yi ------------------------------------------------------------
+    if (tid == 0) {
+      constexpr uint32_t i_wm = umma::idesc_bf16(128, 128, false, false);
+      constexpr uint32_t i_yi = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t km = (ks >> 2) * 16384u + (ks & 3) * 32u, mn = ks * 2048u;
+        const uint64_t dq = umma::smem_desc(aQ + km, 16, 1024);
+        umma::mma_bf16(tm + 0, dq, umma::smem_desc(aK + km, 16, 1024), i_wm, ks > 0);
+        umma::mma_bf16(tm + 256, dq, umma::smem_desc(aSt + mn, 16384, 1024), i_yi, ks > 0);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_bf16(tm + 128, umma::smem_desc(aG + ks * 32u, 16, 1024), umma::smem_desc(aV + ks * 32u, 16, 1024),
+                       i_wm, ks > 0);
+      umma::commit(&ss->mbar[0]);
+    }
+    if (__syncthreads_or(!umma::mbar_wait(&ss->mbar[0], (nchunk - 1 - c) & 1))) {
+      if (tid == 0) atomicExch(&g_m3_device_error, 11);
+      ok = false;
+      break;
+    }
+    umma::fence_after_sync();
+
+    // ---- mask: one decay for Wm and dM, bf16 into their tiles (rows = token) -----------
+#pragma unroll
+    for (int cb = 0; cb < 2; ++cb) {
+      float wv[32], mv[32];
+      const int sb = 64 * half + 32 * cb;
+      umma::tmem_ld32(tm + lane_base + sb, wv);
+      umma::tmem_ld32(tm + lane_base + 128 + sb, mv);
+      umma::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float w8[8], m8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int s = sb + 8 * j + e;
+          float wd = 0.f, md = 0.f;
+          if (s < t) {
+            const float dec = ex2(fminf(A - ss->A[s], 0.f));
+            wd = wv[8 * j + e] * dec;
+            md = mv[8 * j + e] * dec;
+          }
+          w8[e] = wd;
+          m8[e] = md;
+        }
+        *reinterpret_cast<uint4*>(sm + kWm + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(w8);
+        *reinterpret_cast<uint4*>(sm + kDM + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(m8);
+      }
+    }
+    umma::fence_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+
+    // ---- round 2 ----------------------------------------------------------------------------
+    if (tid == 0) {
+      constexpr uint32_t i_ya = umma::idesc_bf16(128, 64, false, true);
+      constexpr uint32_t i_dva = umma::idesc_bf16(128, 64, true, true);
+      constexpr uint32_t i_dq = umma::idesc_bf16(128, 128, false, true);
+      constexpr uint32_t i_dqb = umma::idesc_bf16(128, 128, false, false);
+      constexpr uint32_t i_dk = umma::idesc_bf16(128, 128, true, true);
+      constexpr uint32_t i_dvb = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t km = (ks >> 2) * 16384u + (ks & 3) * 32u, mn = ks * 2048u;
+        umma::mma_bf16(tm + 0, umma::smem_desc(aWm + km, 16, 1024), umma::smem_desc(aV + mn, 16384, 1024), i_ya, ks > 0);
+        umma::mma_bf16(tm + 64, umma::smem_desc(aWm + mn, 16384, 1024), umma::smem_desc(aG + mn, 16384, 1024), i_dva,
+                       ks > 0);
+        umma::mma_bf16(tm + 128, umma::smem_desc(aDM + km, 16, 1024), umma::smem_desc(aK + mn, 16384, 1024), i_dq,
+                       ks > 0);
+        umma::mma_bf16(tm + 320, umma::smem_desc(aDM + mn, 16384, 1024), umma::smem_desc(aQ + mn, 16384, 1024), i_dk,
+                       ks > 0);
+        umma::mma_bf16(tm + 448, umma::smem_desc(aK + km, 16, 1024), umma::smem_desc(aGt + mn, 16384, 1024), i_dvb,
+                       ks > 0);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        umma::mma_bf16(tm + 128, umma::smem_desc(aGe + ks * 32u, 16, 1024), umma::smem_desc(aSt + ks * 32u, 16, 1024),
+                       i_dqb, true);
+        umma::mma_bf16(tm + 320, umma::smem_desc(aVd + ks * 32u, 16, 1024), umma::smem_desc(aGt + ks * 32u, 16, 1024),
+                       i_dqb, true);
+      }
+      umma::commit(&ss->mbar[1]);
+    }
+    if (__syncthreads_or(!umma::mbar_wait(&ss->mbar[1], (nchunk - 1 - c) & 1))) {
+      if (tid == 0) atomicExch(&g_m3_device_error, 12);
+      ok = false;
+      break;
+    }
+    umma::fence_after_sync();
+
+    // ---- epilogue: ybar -> dz, dv ---------------------------------------------------------
+    {
+      float yi[32], ya[32];
+      umma::tmem_ld32(tm + lane_base + 256 + 32 * half, yi);
+      umma::tmem_ld32(tm + lane_base + 32 * half, ya);
+      umma::tmem_wait_ld();
+      if (z) {
+        const __nv_bfloat16* dyr = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tg * a.dy_st.l + 32 * half;
+        const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
+        float* dzr = a.dz + (bh * L + tg) * kP + 32 * half;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 ud = *reinterpret_cast<const uint4*>(dyr + 8 * j);
+          const uint4 uz = *reinterpret_cast<const uint4*>(zr + 8 * j);
+          const uint32_t d4[4] = {ud.x, ud.y, ud.z, ud.w}, z4[4] = {uz.x, uz.y, uz.z, uz.w};
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int i = 8 * j + 2 * e + u;
+              const float vv = u ? bf16hi(vreg[4 * j + e]) : bf16lo(vreg[4 * j + e]);
+              const float zz = u ? bf16hi(z4[e]) : bf16lo(z4[e]);
+              const float dd = u ? bf16hi(d4[e]) : bf16lo(d4[e]);
+              const float ybar = eA * yi[i] + ya[i] + dg * vv;
+              const float sg = sigmoidf_(zz);
+              o[2 * e + u] = dd * ybar * sg * (1.f + zz * (1.f - sg));
+            }
+          }
+          *reinterpret_cast<float4*>(dzr + 8 * j) = make_float4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<float4*>(dzr + 8 * j + 4) = make_float4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+    umma::fence_before_sync();
+    __syncthreads();  // Yi has been read: round 3 may overwrite its columns
+    umma::fence_after_sync();
+    if (tid == 0) {
+      constexpr uint32_t i_dg = umma::idesc_bf16(128, 64, true, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma::mma_bf16(tm + 256, umma::smem_desc(aQ + ks * 2048u, 16384, 1024),
+                       umma::smem_desc(aGe + ks * 2048u, 16384, 1024), i_dg, ks > 0);
+      umma::commit(&ss->mbar[2]);
+    }
+    {
+      float da[32], db[32];
+      umma::tmem_ld32(tm + lane_base + 64 + 32 * half, da);
+      umma::tmem_ld32(tm + lane_base + 448 + 32 * half, db);
+      umma::tmem_wait_ld();
+      float* dvr = a.dv + (bh * L + tg) * kP + 32 * half;
+      const bool last = (tg == L - 1) && a.dfinal_v;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float o[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          o[u] = da[i + u] + erev * db[i + u] + dg * gv[i + u];
+          if (last) o[u] += a.dfinal_v[bh * kP + 32 * half + i + u];
+        }
+        *reinterpret_cast<float4*>(dvr + i) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    }
+
+    // ---- pullback through the rotation (fp32, recomputed q~ / k~), 8 pairs at a time -------
+    float dsc = 0.f, dAp = 0.f;
+    {
+      const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tg * a.q_st.l;
+      const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tg * a.k_st.l;
+      const float dgm = qkd * gam;
+      float* dqrow = a.dq + ((size_t)b * L + tg) * kN;
+      float* dkrow = a.dk + ((size_t)b * L + tg) * kN;
+      float* dus = reinterpret_cast<float*>(sm + kDu) + t * 128;
+      float* dws = reinterpret_cast<float*>(sm + kDw) + t * 128;
+      const bool lastk = (tg == L - 1) && a.dfinal_k;
+#pragma unroll 1
+      for (int sbk = 0; sbk < 4; ++sbk) {
+        const int j0 = 32 * half + 8 * sbk;
+        float dql[8], dqh[8], dkl[8], dkh[8];
+        tmem_ld8(tm + lane_base + 128 + j0, dql);
+        tmem_ld8(tm + lane_base + 128 + 64 + j0, dqh);
+        tmem_ld8(tm + lane_base + 320 + j0, dkl);
+        tmem_ld8(tm + lane_base + 320 + 64 + j0, dkh);
+        umma::tmem_wait_ld();
+        const uint4 uq0 = *reinterpret_cast<const uint4*>(qr + j0), uq1 = *reinterpret_cast<const uint4*>(qr + 64 + j0);
+        const uint4 uk0 = *reinterpret_cast<const uint4*>(kr + j0), uk1 = *reinterpret_cast<const uint4*>(kr + 64 + j0);
+        const uint32_t ql[4] = {uq0.x, uq0.y, uq0.z, uq0.w}, qh[4] = {uq1.x, uq1.y, uq1.z, uq1.w};
+        const uint32_t kl[4] = {uk0.x, uk0.y, uk0.z, uk0.w}, kh[4] = {uk1.x, uk1.y, uk1.z, uk1.w};
+        float* pp = phs + (size_t)t * 64 + j0;
+        float phv[8];
+        {
+          const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
+          phv[0] = p0.x; phv[1] = p0.y; phv[2] = p0.z; phv[3] = p0.w;
+          phv[4] = p1.x; phv[5] = p1.y; phv[6] = p1.z; phv[7] = p1.w;
+        }
+        float dul[8], duh[8], dwl[8], dwh[8], dph[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int j = j0 + r;
+          const float ulo = ((r & 1) ? bf16hi(ql[r >> 1]) : bf16lo(ql[r >> 1])) + a.q_bias[h * kN + j];
+          const float uhi = ((r & 1) ? bf16hi(qh[r >> 1]) : bf16lo(qh[r >> 1])) + a.q_bias[h * kN + 64 + j];
+          const float wlo = ((r & 1) ? bf16hi(kl[r >> 1]) : bf16lo(kl[r >> 1])) + a.k_bias[h * kN + j];
+          const float whi = ((r & 1) ? bf16hi(kh[r >> 1]) : bf16lo(kh[r >> 1])) + a.k_bias[h * kN + 64 + j];
+          float cs = 1.f, sn = 0.f;
+          if (j < Nr) sincos_wrapped(wrap_fast(phv[r]), &sn, &cs);
+          const float qlo = ulo * cs - uhi * sn, qhi = uhi * cs + ulo * sn;
+          const float klo = wlo * cs - whi * sn, khi = whi * cs + wlo * sn;
+          float dklo = dkl[r] * scl, dkhi = dkh[r] * scl;
+          if (lastk) {
+            dklo += a.dfinal_k[bh * kN + j];
+            dkhi += a.dfinal_k[bh * kN + 64 + j];
+          }
+          dul[r] = dql[r] * cs + dqh[r] * sn + dgm * wlo;
+          duh[r] = dqh[r] * cs - dql[r] * sn + dgm * whi;
+          dwl[r] = dklo * cs + dkhi * sn + dgm * ulo;
+          dwh[r] = dkhi * cs - dklo * sn + dgm * uhi;
+          dsc += dkl[r] * klo + dkh[r] * khi;
+          dAp += qlo * dql[r] + qhi * dqh[r] - scl * (klo * dkl[r] + khi * dkh[r]);
+          dph[r] = j < Nr ? (dqh[r] * qlo - dql[r] * qhi) + (dkhi * klo - dklo * khi) : 0.f;
+        }
+        *reinterpret_cast<float4*>(pp) = make_float4(dph[0], dph[1], dph[2], dph[3]);
+        *reinterpret_cast<float4*>(pp + 4) = make_float4(dph[4], dph[5], dph[6], dph[7]);
+        red_add4(dqrow + j0, dul[0], dul[1], dul[2], dul[3]);
+        red_add4(dqrow + j0 + 4, dul[4], dul[5], dul[6], dul[7]);
+        red_add4(dqrow + 64 + j0, duh[0], duh[1], duh[2], duh[3]);
+        red_add4(dqrow + 64 + j0 + 4, duh[4], duh[5], duh[6], duh[7]);
+        red_add4(dkrow + j0, dwl[0], dwl[1], dwl[2], dwl[3]);
+        red_add4(dkrow + j0 + 4, dwl[4], dwl[5], dwl[6], dwl[7]);
+        red_add4(dkrow + 64 + j0, dwh[0], dwh[1], dwh[2], dwh[3]);
+        red_add4(dkrow + 64 + j0 + 4, dwh[4], dwh[5], dwh[6], dwh[7]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {  // per-head rows for the bias reductions
+          const int sw = t & 31;
+          dus[(j0 + r) ^ sw] = dul[r];
+          dus[(64 + j0 + r) ^ sw] = duh[r];
+          dws[(j0 + r) ^ sw] = dwl[r];
+          dws[(64 + j0 + r) ^ sw] = dwh[r];
+        }
+      }
+    }
+    float* part = reinterpret_cast<float*>(sm + kScrPart);  // [2 halves][2][128]: dscale, dA
+    part[(half * 2 + 0) * 128 + t] = dsc;
+    part[(half * 2 + 1) * 128 + t] = dAp;
+    if (half == 0) reinterpret_cast<float*>(sm + kScrDtb)[t] = dt;
+    __syncthreads();
+
+    // ---- bias column sums; angle adjoints (suffix over tokens) ------------------------------
+    {
+      const int n = tid & 127;
+      const float* src = reinterpret_cast<const float*>(sm + (half ? kDw : kDu));
+      float acc = 0.f;
+#pragma unroll 8
+      for (int tt = 0; tt < 128; ++tt) acc += src[tt * 128 + (n ^ (tt & 31))];
+      bias_acc += acc;
+    }
+    {
+      const int g = warp;
+      const bool grot = 8 * g < Nr;
+      float* dthp = reinterpret_cast<float*>(sm + kScrTh);  // [8][128]
+      const float* dts = reinterpret_cast<const float*>(sm + kScrDtb);
+#pragma unroll 1
+      for (int i = 3; i >= 0; --i) {
+        const int tt = lane + 32 * i, tgl = t0 + tt;
+        float share = 0.f;
+        if (grot) {
+          const float* pp = phs + (size_t)tt * 64 + 8 * g;
+          const float4 lo = *reinterpret_cast<const float4*>(pp);
+          const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+          const float dp[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+          const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g;
+          const float4 alo = *reinterpret_cast<const float4*>(ap);
+          const float4 ahi = *reinterpret_cast<const float4*>(ap + 4);
+          const float an[8] = {alo.x, alo.y, alo.z, alo.w, ahi.x, ahi.y, ahi.z, ahi.w};
+          float dan[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float sfx = warp_suffix_scan(dp[r]);
+            const float dth = dcarry8[r] + sfx;
+            dcarry8[r] += __shfl_sync(0xffffffffu, sfx, 0);
+            const float th = tanh_acc(an[r]);
+            dan[r] = dth * kPi * dts[tt] * (1.f - th * th);
+            share += dth * th * kPi;
+          }
+          float* dap = a.dangles + ((size_t)b * L + tgl) * Nr + 8 * g;
+          red_add4(dap, dan[0], dan[1], dan[2], dan[3]);
+          red_add4(dap + 4, dan[4], dan[5], dan[6], dan[7]);
+        }
+        dthp[g * 128 + tt] = share;
+      }
+    }
+    __syncthreads();
+
+    // ---- per-token scalars: dadt (suffix of dA + the A_last term), preprocess adjoint -------
+    {
+      const float dscl = part[t] + part[256 + t];
+      const float dA = part[128 + t] + part[384 + t];
+      // suffix sum of dA over the chunk's 128 tokens (warps 0..3 own 32 tokens each)
+      const float sfx = warp_suffix_scan(dA);
+      if (half == 0 && lane == 0) ss->wtot[warp & 3] = sfx;
+      __syncthreads();
+      float dadt = sfx + alast;
+      for (int w = (warp & 3) + 1; w < 4; ++w) dadt += ss->wtot[w];
+      const float dscp = __shfl_up_sync(0xffffffffu, dscl, 1);
+      float dth = 0.f;
+      {
+        const float* dthp = reinterpret_cast<const float*>(sm + kScrTh);
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) dth += dthp[gg * 128 + t];
+      }
+      if (half == 0) {
+        float prev = dscp;
+        if (lane == 0) prev = t > 0 ? part[t - 1] + part[256 + t - 1] : 0.f;
+        const float dgam = qkd * uwt;
+        if (a.d_skip) dD_acc += qkd;
+        const float ddt = (dgam + dscl) * lam + prev * (1.f - lam) + dadt * av + dth;
+        const float dlam = (dgam + dscl) * dt - prev * dt;
+        const float sgd = sigmoidf_(a.dt_raw[ro] + dtb);
+        const size_t od = ((size_t)b * L + tg) * H + h;
+        a.ddt_raw[od] = ddt * sgd;
+        ddtb_acc += ddt * sgd;
+        const bool open = -heavy_tail(ar) < -a.a_floor;
+        const float htp = ar >= 0.f ? 1.f : 1.f / ((1.f - ar) * (1.f - ar));
+        a.da_raw[od] = open ? -(dadt * dt) * htp : 0.f;
+        a.dtrap_raw[od] = dlam * lam * (1.f - lam);
+        if (t == kC - 1 && tg + 1 < L) {
+          // scale of this chunk's last token reaches dt / lambda of the next chunk's first
+          // token, whose gradients this block wrote one iteration earlier
+          const size_t on = ro + a.raw_st.l, odn = od + H;
+          const float sgn = sigmoidf_(a.dt_raw[on] + dtb);
+          const float e_dt = dscl * (1.f - lamn) * sgn;
+          a.ddt_raw[odn] += e_dt;
+          ddtb_acc += e_dt;
+          a.dtrap_raw[odn] += -dscl * dtn * lamn * (1.f - lamn);
+        }
+      }
+    }
+
+    // ---- round 3 result: G <- exp2(A_last) G + dG; A_last term of the previous chunk -------
+    if (__syncthreads_or(!umma::mbar_wait(&ss->mbar[2], (nchunk - 1 - c) & 1))) {
+      if (tid == 0) atomicExch(&g_m3_device_error, 13);
+      ok = false;
+      break;
+    }
+    umma::fence_after_sync();
+    {
+      float dG[32];
+      umma::tmem_ld32(tm + lane_base + 256 + 32 * half, dG);
+      umma::tmem_wait_ld();
+      const float eAl = exp2f(Alast);
+      float partS = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) G[i] = G[i] * eAl + dG[i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint4*>(sm + kGt + umma::sw128_off(t, 4 * half + j)) = pack8(G + 8 * j);
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j));
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) partS += G[8 * j + 2 * e] * bf16lo(w4[e]) + G[8 * j + 2 * e + 1] * bf16hi(w4[e]);
+      }
+      const float tot = cta_sum(partS, ss);
+      if (tid == 0) ss->alast = tot;
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+  }
+
+  if (ok) {
+    // ---- seeds (kernel_bwd.py:636-646), angle carry, per-head reductions ------------------
+    if (a.seed_ssm) {
+      const size_t o0 = (size_t)b * a.raw_st.b + (size_t)h * a.raw_st.h;
+      const float dt0 = softplusf(a.dt_raw[o0] + dtb), lam0 = sigmoidf_(a.trap_raw[o0]);
+      const float coef = dt0 * (1.f - lam0);
+      const float kp = a.seed_k[bh * kN + t];
+      float pk = 0.f, pc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int p = 32 * half + i;
+        a.dseed_ssm[(bh * kP + p) * kN + t] = G[i];
+        const float vp = a.seed_v[bh * kP + p];
+        pk += G[i] * vp;
+        pc += G[i] * vp * kp;
+        atomicAdd(a.dseed_v + bh * kP + p, coef * G[i] * kp);
+      }
+      atomicAdd(a.dseed_k + bh * kN + t, coef * pk);
+      const float dcoef = cta_sum(pc, ss);
+      if (tid == 0) {
+        const size_t od = (size_t)b * L * H + h;
+        const float sg = sigmoidf_(a.dt_raw[o0] + dtb);
+        const float e_dt = dcoef * (1.f - lam0) * sg;
+        a.ddt_raw[od] += e_dt;
+        ddtb_acc += e_dt;
+        a.dtrap_raw[od] += -dcoef * dt0 * lam0 * (1.f - lam0);
+      }
+    }
+    if (a.dseed_phi && lane == 0 && 8 * warp < Nr)
+#pragma unroll
+      for (int r = 0; r < 8; ++r) a.dseed_phi[bh * Nr + 8 * warp + r] = dcarry8[r];
+    atomicAdd((half ? a.dk_bias : a.dq_bias) + h * kN + t, bias_acc);
+    const float dD = cta_sum(dD_acc, ss);
+    const float ddb = cta_sum(ddtb_acc, ss);
+    if (tid == 0) {
+      if (a.d_skip) atomicAdd(a.dd_skip + h, dD);
+      atomicAdd(a.ddt_bias + h, ddb);
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tm, 512);
+}
+
+}  // namespace tcb
+}  // namespace m3

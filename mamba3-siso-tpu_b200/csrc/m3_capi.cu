@@ -173,6 +173,14 @@ int m3_siso_bwd(const M3BwdArgs* args, void* stream) {
     cudaMemsetAsync(a.dangles, 0, (size_t)d.batch * d.seqlen * d.n_angles * sizeof(float), s);
   }
   if ((rc = check_launch("m3_siso_bwd: zeroing")) != M3_OK) return rc;
+  if (a.kernel < M3_KERNEL_AUTO || a.kernel > M3_KERNEL_TENSORCORE)
+    return set_error(M3_ERR_ARG, "kernel must be AUTO, GENERIC or TENSORCORE");
+  const bool tc_ok = bwd_tc_eligible(a);
+  if (a.kernel == M3_KERNEL_TENSORCORE && !tc_ok)
+    return set_error(M3_ERR_UNSUPPORTED,
+                     "tensor-core backward needs the raw boundary, bf16 I/O, bf16 policy, N=128, P=64, "
+                     "chunk % 128 == 0, n_angles a multiple of 8 and <= 64, and 16-byte aligned rows");
+  if (tc_ok && a.kernel != M3_KERNEL_GENERIC) return launch_bwd_tc(a, s);
   return launch_bwd_simt(a, s);
 }
 

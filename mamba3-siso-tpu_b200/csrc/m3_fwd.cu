@@ -2,6 +2,7 @@
 // shape, the generic CUDA-core kernel for everything else.
 #include "m3_fwd_simt.cuh"
 #include "m3_fwd_tc.cuh"
+#include "m3_bwd_tc.cuh"
 #include "m3_internal.h"
 
 namespace m3 {
@@ -44,20 +45,31 @@ static bool fwd_tc_eligible(const M3FwdArgs& a) {
   return true;
 }
 
-static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s) {
-  auto* kern = a.raw ? tc::fwd_tc_kernel<true> : tc::fwd_tc_kernel<false>;
-  static bool attr_done[2][64] = {};
+static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s, const tc::TcStates* states = nullptr) {
+  const int mode = (a.raw ? 1 : 0) + (states ? 2 : 0);
+  decltype(&tc::fwd_tc_kernel<true, false>) kerns[4] = {tc::fwd_tc_kernel<false, false>, tc::fwd_tc_kernel<true, false>,
+                                                         tc::fwd_tc_kernel<false, true>, tc::fwd_tc_kernel<true, true>};
+  auto* kern = kerns[mode];
+  static bool attr_done[4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[a.raw][dev]) {
+  if (dev < 64 && !attr_done[mode][dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes) != cudaSuccess)
       return check_launch("fwd_tc: cudaFuncSetAttribute");
-    attr_done[a.raw][dev] = true;
+    attr_done[mode][dev] = true;
   }
   const int nseq = a.dims.batch * a.dims.nheads;
-  kern<<<(nseq + 1) / 2, tc::kThreads, tc::kSmemBytes, s>>>(a);
+  kern<<<(nseq + 1) / 2, tc::kThreads, tc::kSmemBytes, s>>>(a, states ? *states : tc::TcStates{nullptr, nullptr});
   return check_launch("m3_siso_fwd (tensor core)");
 }
+
+// The backward's recompute sweep: chunk-start state tiles and angle carries only.
+int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s) {
+  const tc::TcStates st{tiles, phis};
+  return run_fwd_tc(a, s, &st);
+}
+
+bool fwd_tc_eligible_public(const M3FwdArgs& a) { return fwd_tc_eligible(a); }
 
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   const bool tc_ok = fwd_tc_eligible(a);
@@ -73,6 +85,75 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   return mmb ? run_fwd<N_, P_, float, true>(a, s) : run_fwd<N_, P_, float, false>(a, s);
   M3_DISPATCH_NP(a.dims.state_dim, a.dims.headdim, X);
 #undef X
+}
+
+// ---- backward on tensor cores ------------------------------------------------------------
+static size_t tc_tiles_bytes(const M3Dims& d) {
+  return (size_t)d.batch * d.nheads * (d.seqlen / tc::kC + 1) * 16384u;
+}
+static size_t tc_phis_bytes(const M3Dims& d) {
+  return (size_t)d.batch * d.nheads * (d.seqlen / tc::kC) * d.n_angles * sizeof(float);
+}
+size_t bwd_tc_workspace_bytes(const M3Dims& d) {
+  return tc_tiles_bytes(d) + tc_phis_bytes(d) + (size_t)d.batch * d.nheads * tcb::kC * 64 * sizeof(float) + 256;
+}
+
+bool bwd_tc_eligible(const M3BwdArgs& a) {
+  if (!a.raw) return false;
+  M3FwdArgs f{};
+  f.dims = a.dims;
+  f.io_dtype = a.io_dtype;
+  f.policy = a.policy;
+  f.raw = 1;
+  f.q = a.q; f.k = a.k; f.v = a.v; f.z = a.z;
+  f.q_st = a.q_st; f.k_st = a.k_st; f.v_st = a.v_st; f.z_st = a.z_st;
+  f.angles = a.angles; f.ang_st = a.ang_st;
+  f.q_bias = a.q_bias; f.k_bias = a.k_bias;
+  if (!fwd_tc_eligible(f)) return false;
+  auto rows_ok = [](const void* p, const M3Strides& s) {
+    return al16(p) && s.b % 8 == 0 && s.l % 8 == 0 && s.h % 8 == 0;
+  };
+  if (!rows_ok(a.dy, a.dy_st)) return false;
+  if (!al16(a.dq) || !al16(a.dk) || !al16(a.dv) || (a.dz && !al16(a.dz)) || !al16(a.dangles)) return false;
+  return true;
+}
+
+int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s) {
+  const M3Dims& d = a.dims;
+  uint8_t* ws = (uint8_t*)a.workspace;
+  uint8_t* tiles = ws;
+  float* phis = (float*)(ws + tc_tiles_bytes(d));
+  float* scratch = (float*)(ws + tc_tiles_bytes(d) + tc_phis_bytes(d));
+  // sweep 1: recompute the chunk-start states (forward kernel, states-only mode)
+  M3FwdArgs f{};
+  f.dims = d;
+  f.io_dtype = a.io_dtype;
+  f.policy = a.policy;
+  f.raw = 1;
+  f.a_floor = a.a_floor;
+  f.q = a.q; f.k = a.k; f.v = a.v;
+  f.q_st = a.q_st; f.k_st = a.k_st; f.v_st = a.v_st;
+  f.dt_raw = a.dt_raw; f.a_raw = a.a_raw; f.trap_raw = a.trap_raw; f.raw_st = a.raw_st;
+  f.angles = a.angles; f.ang_st = a.ang_st; f.dt_bias = a.dt_bias;
+  f.q_bias = a.q_bias; f.k_bias = a.k_bias; f.d_skip = a.d_skip;
+  f.seed_ssm = a.seed_ssm; f.seed_k = a.seed_k; f.seed_v = a.seed_v; f.seed_phi = a.seed_phi;
+  int rc = launch_fwd_states_tc(f, tiles, phis, s);
+  if (rc != M3_OK) return rc;
+  if (a.seed_ssm) {
+    cudaMemsetAsync(a.dseed_k, 0, (size_t)d.batch * d.nheads * d.state_dim * sizeof(float), s);
+    cudaMemsetAsync(a.dseed_v, 0, (size_t)d.batch * d.nheads * d.headdim * sizeof(float), s);
+  }
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    if (cudaFuncSetAttribute(tcb::bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcb::kSmemBytes) !=
+        cudaSuccess)
+      return check_launch("bwd_tc: cudaFuncSetAttribute");
+    attr_done[dev] = true;
+  }
+  tcb::bwd_tc_kernel<<<d.batch * d.nheads, tcb::kThreads, tcb::kSmemBytes, s>>>(a, tiles, phis, scratch);
+  return check_launch("m3_siso_bwd (tensor core)");
 }
 
 int read_device_error(int reset) {

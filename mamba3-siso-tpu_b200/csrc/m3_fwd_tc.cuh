@@ -100,8 +100,16 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return u;
 }
 
-template <bool RAW>
-__global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) {
+// Outputs of the states-only mode used by the backward's recompute sweep: the bf16 state
+// tile image (the layout the backward's tensor-core operands use) at every chunk start
+// plus the final state, and the rotary-angle carry at every chunk start.
+struct TcStates {
+  uint8_t* tiles;  // (B*H, nchunk + 1, 16 KB)
+  float* phis;     // (B*H, nchunk, Nr)
+};
+
+template <bool RAW, bool STATES>
+__global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, const TcStates so) {
   extern __shared__ uint8_t smraw[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smraw + 1023) & ~(uintptr_t)1023);
   CtaSmall* cs = (CtaSmall*)(base + 2 * kSlotBytes);
@@ -230,9 +238,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
 #ifdef M3_TC_TIMING
     long long tmark_ = clock64();
 #endif
+    auto dump_state_tile = [&](int cc) {
+      uint4* dst = reinterpret_cast<uint4*>(so.tiles + (bh * (nchunk + 1) + cc) * 16384u);
+      const uint4* src = reinterpret_cast<const uint4*>(sm + kSt);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) dst[ltid + kSlotThreads * m] = src[ltid + kSlotThreads * m];
+    };
     for (int c = 0; c < nchunk && ok; ++c) {
       const int t0 = c * kC;
       const int tg = t0 + t;  // this thread's token (row roles)
+      if constexpr (STATES) {
+        dump_state_tile(c);
+        if (RAW && lane == 0 && 8 * lwarp < Nr)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) so.phis[(bh * nchunk + c) * Nr + 8 * lwarp + r] = carry8[r];
+      }
       // ---- phase 1: per-token scalars (raw values were loaded during the last chunk) ---
       float dt = 0.f, adt, gam, scl;
       if (RAW) {
@@ -339,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
               ok_hi[r] = whi[u] * cs[r] + wlo[u] * sn[r];
             }
           }
-          if (tgl == L - 1) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
+          if (tgl == L - 1 && a.final_k) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
             float* fk = a.final_k + bh * kN + 8 * g;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
@@ -410,9 +430,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
         for (int ks = 0; ks < 8; ++ks) {
           const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
           const uint32_t mn = ks * 2048u;
-          const uint64_t dq = umma::smem_desc(sQ + kmaj, 16, 1024);
-          umma::mma_bf16(tm + 0, dq, umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
-          umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + mn, 16384, 1024), id_yi, ks > 0);
+          if constexpr (!STATES) {
+            const uint64_t dq = umma::smem_desc(sQ + kmaj, 16, 1024);
+            umma::mma_bf16(tm + 0, dq, umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
+            umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + mn, 16384, 1024), id_yi, ks > 0);
+          }
           umma::mma_bf16(tm + 192, umma::smem_desc(sK + mn, 16384, 1024), umma::smem_desc(sVd + mn, 16384, 1024),
                          id_ds, ks > 0);
         }
@@ -426,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       umma::fence_after_sync();
 
       // the khat tile is free until the next chunk: stage this thread's z row pieces there
-      if (z) {
+      if (!STATES && z) {
         const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
 #pragma unroll
         for (int j = 0; j < 4; ++j) umma::cp_async16(sK + umma::sw128_off(t, 4 * half + j), zr + 8 * j);
@@ -457,6 +479,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
         if (half == 0) reinterpret_cast<float*>(sm + kVd + kScrA)[t] = A;
       }
       slot_sync(slot);
+      if constexpr (STATES) {  // nothing else of this chunk is needed: fetch the next one
+        if (c + 1 < nchunk) {
+          prefetch_qv(c + 1);
+          prefetch_k(c + 1);
+          load_scalars(c + 1);
+        }
+        continue;
+      }
       // ---- phase 5b: decay mask of S -> bf16 into the q~ tile -----------------------------
       {
         const float* As = reinterpret_cast<const float*>(sm + kVd + kScrA);
@@ -557,10 +587,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a) 
       M3_TC_MARK(6);
     }
 
+    if constexpr (STATES) {
+      slot_sync(slot);
+      dump_state_tile(nchunk);
+    }
     // ---- final state (kernel_fwd.py:189-201) ---------------------------------------------
+    if (a.final_ssm)
 #pragma unroll 8
-    for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = st[i];
-    if (ltid < kP) {
+      for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = st[i];
+    if (a.final_v && ltid < kP) {
       const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(L - 1) * a.v_st.l;
       a.final_v[bh * kP + ltid] = __bfloat162float(vr[ltid]);
     }

@@ -19,6 +19,11 @@ bool supported_np(int n, int p);
 
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s);
 int read_device_error(int reset);
+int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s);
+bool fwd_tc_eligible_public(const M3FwdArgs& a);
+size_t bwd_tc_workspace_bytes(const M3Dims& d);
+bool bwd_tc_eligible(const M3BwdArgs& a);
+int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s);
 int launch_bwd_simt(const M3BwdArgs& a, cudaStream_t s);
 int launch_decode(const M3DecodeArgs& a, cudaStream_t s);
 size_t bwd_workspace_bytes(const M3Dims& d);

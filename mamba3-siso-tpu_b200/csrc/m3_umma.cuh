@@ -101,11 +101,13 @@ __device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
 }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
-// Wait for phase `parity` of `mbar` to complete, giving up after `limit` polls.  Returns
-// false on time-out (the caller records an error and winds down; no thread spins forever).
-__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint32_t limit = (1u << 26)) {
+// Wait for phase `parity` of `mbar` to complete, giving up after about `limit_cycles`
+// SM clock cycles (default ~2 s).  Returns false on time-out (the caller records an error
+// and winds down; no thread spins forever).
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, long long limit_cycles = 4000000000LL) {
   const uint32_t a = smem_u32(mbar);
-  for (uint32_t i = 0; i < limit; ++i) {
+  const long long t0 = clock64();
+  while (true) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -115,8 +117,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity, uint3
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
+    if (clock64() - t0 > limit_cycles) return false;
   }
-  return false;
 }
 
 // ---- cp.async: 16-byte global -> shared copies that do not occupy registers -----------

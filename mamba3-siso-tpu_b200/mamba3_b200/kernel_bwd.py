@@ -136,7 +136,7 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
                       d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                       dfinal_ssm=None, dfinal_k=None, dfinal_v=None, dfinal_phi=None,
                       a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
-                      workspace=None) -> RawGrads:
+                      workspace=None, kernel: str = "auto") -> RawGrads:
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape
@@ -183,6 +183,7 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     a.ddt_raw, a.da_raw, a.dtrap_raw, a.dangles, a.ddt_bias = T.ptr(ddt), T.ptr(da), T.ptr(dtr), T.ptr(dang), T.ptr(ddtb)
     a.dq_bias, a.dk_bias, a.dd_skip = T.ptr(dqb), T.ptr(dkb), T.ptr(ddsk)
     a.dseed_ssm, a.dseed_k, a.dseed_v, a.dseed_phi = T.ptr(dss), T.ptr(dsk_), T.ptr(dsv), T.ptr(dsp)
+    a.kernel = {"auto": C.M3_KERNEL_AUTO, "generic": C.M3_KERNEL_GENERIC, "tensorcore": C.M3_KERNEL_TENSORCORE}[kernel]
     ws, need = _workspace(a.dims, dev, workspace)
     a.workspace, a.workspace_bytes = T.ptr(ws), need
     C.check(C.lib().m3_siso_bwd(a, T.stream_handle(dev)))

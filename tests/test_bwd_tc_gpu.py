@@ -1,0 +1,61 @@
+"""The tcgen05 tensor-core backward (raw boundary, bf16 I/O and operands, N=128, P=64)
+against exact float64 gradients of the same bf16-valued inputs (normwise, as for the
+generic kernel's bf16 test) and against the generic kernel."""
+
+import pytest
+import torch
+
+from tests.test_bwd_gpu import BF16_GRAD_TOL, RAW_NAMES, _normwise, _raw_case, _raw_kernel_grads, _raw_oracle_grads
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    from mamba3_b200 import _capi as C
+
+    C.lib().m3_device_error(1)
+    yield
+    assert C.lib().m3_device_error(1) == 0
+
+
+def _kernel(x, st, cots, chunk, kernel):
+    from mamba3_b200 import kernel_bwd as KB
+    from tests.gpu_common import dev
+
+    dfs, dfk, dfv, dfp = cots
+    io = lambda t: dev(t, torch.bfloat16)
+    return KB.siso_backward_raw(
+        io(x["dy"]), io(x["q"]), io(x["k"]), io(x["v"]), dev(x["dt_raw"]), dev(x["a_raw"]), dev(x["trap_raw"]),
+        dev(x["angles"]), dev(x["dt_bias"]), dev(x["q_bias"]), dev(x["k_bias"]), d_skip=dev(x["d_skip"]),
+        z=io(x["z"]), seed_ssm=None if st is None else dev(st.ssm), seed_k=None if st is None else dev(st.k),
+        seed_v=None if st is None else dev(st.v), seed_phi=None if st is None else dev(st.phi),
+        dfinal_ssm=dev(dfs), dfinal_k=dev(dfk), dfinal_v=dev(dfv), dfinal_phi=dev(dfp), chunk=chunk,
+        dtype_policy="bf16", kernel=kernel)
+
+
+def _pairs(g):
+    return dict(q=g.dq, k=g.dk, v=g.dv, dt_raw=g.ddt_raw, a_raw=g.da_raw, trap_raw=g.dtrap_raw, angles=g.dangles,
+                dt_bias=g.ddt_bias, q_bias=g.dq_bias, k_bias=g.dk_bias, d_skip=g.dd_skip, z=g.dz)
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 256, 128, 64, 32, 128), (1, 2, 384, 128, 64, 64, 128)])
+@pytest.mark.parametrize("seeded", [False, True])
+def test_tc_backward_vs_exact_and_generic(shape, seeded):
+    x, st, cots = _raw_case(shape, seeded)
+    r = lambda t: t.to(torch.bfloat16).double()
+    xr = dict(x)
+    xr["dy"] = r(x["dy"])
+    leaves, sl = _raw_oracle_grads(xr, st, cots, shape[-1], policy="f32", cast=r)
+    g_tc = _kernel(xr, st, cots, shape[-1], "tensorcore")
+    g_gen = _kernel(xr, st, cots, shape[-1], "generic")
+    pt, pg = _pairs(g_tc), _pairs(g_gen)
+    errs = {k: _normwise(pt[k], leaves[k].grad) for k in RAW_NAMES}
+    vs_gen = {k: _normwise(pt[k], pg[k]) for k in RAW_NAMES}
+    if seeded:
+        errs.update(seed_ssm=_normwise(g_tc.dseed_ssm, sl["ssm"].grad), seed_k=_normwise(g_tc.dseed_k, sl["k"].grad),
+                    seed_v=_normwise(g_tc.dseed_v, sl["v"].grad), seed_phi=_normwise(g_tc.dseed_phi, sl["phi"].grad))
+    bad = {k: e for k, e in errs.items() if not e < BF16_GRAD_TOL}
+    assert not bad, f"normwise errors vs exact above {BF16_GRAD_TOL}: {bad} (all {errs}; vs generic {vs_gen})"
+    bad = {k: e for k, e in vs_gen.items() if not e < BF16_GRAD_TOL}
+    assert not bad, f"normwise differences vs the generic kernel: {bad}"
