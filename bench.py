@@ -350,14 +350,14 @@ def bench_decode(steps, warmup, world, rank, peaks, batch=256):
             "kernel_bytes_per_layer": byts, "launches_per_step": cfg.n_layers}
 
 
-def cpu_baseline_sample(threads=None):
+def cpu_baseline_sample(threads=None, seconds=10.0):
     """The oracle restatement (``oracle/``) on a bounded slice of configs[1]'s forward: all
     32 heads, N=128 P=64 Nr=64 chunk=128, L=256 tokens, float32, on the host cores."""
     from oracle import siso_oracle as O
 
     threads = threads or os.cpu_count()
     torch.set_num_threads(threads)
-    c = dict(CFG2, B=1, L=256)
+    c = dict(CFG2, B=1, L=1024)
     g = torch.Generator().manual_seed(0)
     B, H, L, N, P, Nr = c["B"], c["H"], c["L"], c["N"], c["P"], c["Nr"]
     f = torch.float32
@@ -384,10 +384,10 @@ def cpu_baseline_sample(threads=None):
         run()
         n += 1
         el = time.perf_counter() - t0
-        if el > 8.0 or n >= 50:
+        if el > seconds:
             break
     return {"value": B * L * n / el, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"oracle siso_segment fp32, B=1 H=32 L=256 N=128 P=64 Nr=64 chunk=128, {n} runs in {el:.1f}s"}
+            "sample": f"oracle siso_segment fp32, B=1 H=32 L=1024 N=128 P=64 Nr=64 chunk=128, {n} runs in {el:.1f}s"}
 
 
 # ----------------------------------------------------------------------------------------
@@ -399,7 +399,7 @@ def run_reference(args, world, rank):
     cb = None
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline_sample()
+        r = cpu_baseline_sample(seconds=4.0)
         if i >= args.warmup:
             vals.append(r["value"])
         cb = r
@@ -441,13 +441,13 @@ def main():
     out = {}
     with ClockSampler(torch.cuda.current_device()) as clk:
         fwd, _ = bench_fwd(c, args.steps, args.warmup, world, rank, peaks)
+        if "e2e" in what:
+            out["e2e"] = bench_e2e(c, max(2, args.steps // 2), args.warmup, world, rank)
+        if "fwdbwd" in what:
+            out["fwd_bwd"] = bench_fwd_bwd(c, max(2, args.steps // 2), args.warmup, world, rank)
+        if "decode" in what:
+            out["decode"] = bench_decode(args.steps, args.warmup, world, rank, peaks)
     clocks = clk.summary()
-    if "e2e" in what:
-        out["e2e"] = bench_e2e(c, max(2, args.steps // 2), args.warmup, world, rank)
-    if "fwdbwd" in what:
-        out["fwd_bwd"] = bench_fwd_bwd(c, max(2, args.steps // 2), args.warmup, world, rank)
-    if "decode" in what:
-        out["decode"] = bench_decode(args.steps, args.warmup, world, rank, peaks)
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
 
     if rank != 0:
@@ -480,7 +480,7 @@ def main():
                                 "frac": fwd["tflops"] / peaks["bf16_tflops"],
                                 "flops_per_launch": fwd["flops"]}},
         "gpu_launches": fwd["launches"],
-        "clocks": clocks,
+        "clocks": dict(clocks, sampled="whole timed run (fwd, e2e, fwd+bwd, decode sections)"),
     }
     if "e2e" in out:
         e = out["e2e"]
