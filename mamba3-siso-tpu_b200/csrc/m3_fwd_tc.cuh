@@ -152,9 +152,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
     bool ok = true;
 
     // ---- initial state: registers hold St[n = t][p = 32 half + i] (fp32) ------------
-    float st[32];
+    // The fp32 state lives in TMEM columns [192, 256) of the slot (lane n = t, columns
+    // 32 half ..): the state-update MMA accumulates onto it after the threads have scaled
+    // it by exp2(A_last) in place.  A bf16 copy in the St tile feeds the readout MMA.
     float carry8[8];
     {
+      float st[32];
       float coef = 0.f;
       if (a.seed_ssm) {
         if (RAW) {
@@ -173,10 +176,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(st + 8 * j);
+      umma::tmem_st32(tm + lane_base + 192 + 32 * half, st);
+      umma::tmem_wait_st();
 #pragma unroll
       for (int r = 0; r < 8; ++r)  // angle carry of this warp's rotary group (raw boundary)
         carry8[r] = (RAW && a.seed_phi && 8 * lwarp + r < Nr) ? a.seed_phi[bh * Nr + 8 * lwarp + r] : 0.f;
     }
+    umma::fence_before_sync();
     slot_sync(slot);
 
     // Raw q / k rows of chunk `cc` straight into the q~ / khat tiles (K-major, swizzled)
@@ -415,6 +421,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
           *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + j)) = d;
         }
       }
+      // scale the TMEM state by exp2(A_last) so the update MMA can accumulate onto it; the
+      // chunk-start state residual is this state before scaling
+      {
+        float sv[32];
+        umma::tmem_ld32(tm + lane_base + 192 + 32 * half, sv);
+        umma::tmem_wait_ld();
+        if (a.chunk_states && c % chunk_sub == 0) {
+          const int nc = L / a.dims.chunk, ci = c / chunk_sub;
+          const size_t sb = ((bh * nc + ci) * kP) * kN;
+#pragma unroll 8
+          for (int i = 0; i < 32; ++i) {
+            const size_t o = sb + (size_t)(32 * half + i) * kN + t;
+            if (a.chunk_states_dtype == M3_DTYPE_BF16) ((__nv_bfloat16*)a.chunk_states)[o] = __float2bfloat16_rn(sv[i]);
+            else ((float*)a.chunk_states)[o] = sv[i];
+          }
+        }
+        const float eAl = exp2f(Alast);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[i] *= eAl;
+        umma::tmem_st32(tm + lane_base + 192 + 32 * half, sv);
+        umma::tmem_wait_st();
+      }
       umma::fence_async_smem();
       umma::fence_before_sync();
       slot_sync(slot);
@@ -436,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
             umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + mn, 16384, 1024), id_yi, ks > 0);
           }
           umma::mma_bf16(tm + 192, umma::smem_desc(sK + mn, 16384, 1024), umma::smem_desc(sVd + mn, 16384, 1024),
-                         id_ds, ks > 0);
+                         id_ds, true);
         }
         umma::commit(&ss->mbar[0]);
       }
@@ -455,27 +483,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       }
       umma::cp_async_commit();
       M3_TC_MARK(4);
-      // ---- phase 5a: state update (St lane n = t, columns 32 half ..) ---------------------
+      // ---- phase 5a: the updated state -> bf16 St tile for the next chunk's readout --------
       {
-        if (a.chunk_states && c % chunk_sub == 0) {
-          const int nc = L / a.dims.chunk, ci = c / chunk_sub;
-          const size_t sb = ((bh * nc + ci) * kP) * kN;
-#pragma unroll 8
-          for (int i = 0; i < 32; ++i) {
-            const size_t o = sb + (size_t)(32 * half + i) * kN + t;
-            if (a.chunk_states_dtype == M3_DTYPE_BF16) ((__nv_bfloat16*)a.chunk_states)[o] = __float2bfloat16_rn(st[i]);
-            else ((float*)a.chunk_states)[o] = st[i];
-          }
-        }
-        float d[32];
-        umma::tmem_ld32(tm + lane_base + 192 + 32 * half, d);
+        float sv[32];
+        umma::tmem_ld32(tm + lane_base + 192 + 32 * half, sv);
         umma::tmem_wait_ld();
-        const float eAl = exp2f(Alast);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) st[i] = st[i] * eAl + d[i];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(st + 8 * j);
+          *reinterpret_cast<uint4*>(sm + kSt + umma::sw128_off(t, 4 * half + j)) = pack8(sv + 8 * j);
         if (half == 0) reinterpret_cast<float*>(sm + kVd + kScrA)[t] = A;
       }
       slot_sync(slot);
@@ -592,9 +607,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       dump_state_tile(nchunk);
     }
     // ---- final state (kernel_fwd.py:189-201) ---------------------------------------------
-    if (a.final_ssm)
+    if (a.final_ssm) {
+      float sv[32];
+      umma::fence_after_sync();
+      umma::tmem_ld32(tm + lane_base + 192 + 32 * half, sv);
+      umma::tmem_wait_ld();
 #pragma unroll 8
-      for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = st[i];
+      for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = sv[i];
+    }
     if (a.final_v && ltid < kP) {
       const __nv_bfloat16* vr = v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(L - 1) * a.v_st.l;
       a.final_v[bh * kP + ltid] = __bfloat162float(vr[ltid]);
