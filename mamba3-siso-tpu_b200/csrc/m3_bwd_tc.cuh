@@ -153,6 +153,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float bias_acc = 0.f, dD_acc = 0.f, ddtb_acc = 0.f;
   __syncthreads();
 
+#ifdef M3_TC_TIMING
+  const int ltid = tid;
+  long long tmark_ = clock64();
+#endif
   for (int c = nchunk - 1; c >= 0 && ok; --c) {
     const int t0 = c * kC, tg = t0 + t;
     const float alast = ss->alast;
@@ -235,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     umma::cp_async_wait_all();
     __syncthreads();
+    M3_TC_MARK(8);
 
     // ---- P1: cumulative angles (from the recorded carry) and rotation; phi to scratch ----
     {
@@ -312,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uws[g * 128 + tt] = uw;
       }
     }
+    M3_TC_MARK(9);
     // ---- P2: dqk_diag = g.v (halves), v exp2(A_last - A) tile -------------------------
     uint32_t vreg[16];
     {
@@ -346,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float dg = uwt * gam + Dh;
     const float qkd = reinterpret_cast<const float*>(sm + kScrQkd)[t] + reinterpret_cast<const float*>(sm + kScrQkd)[128 + t];
 
+    M3_TC_MARK(10);
     // ---- round 1: Wm, dM, Yi ------------------------------------------------------------
     if (tid == 0) {
       constexpr uint32_t i_wm = umma::idesc_bf16(128, 128, false, false);
@@ -370,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     umma::fence_after_sync();
 
+    M3_TC_MARK(11);
     // ---- mask: one decay for Wm and dM, bf16 into their tiles (rows = token) -----------
 #pragma unroll
     for (int cb = 0; cb < 2; ++cb) {
@@ -402,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     umma::fence_after_sync();
 
+    M3_TC_MARK(12);
     // ---- round 2 ----------------------------------------------------------------------------
     if (tid == 0) {
       constexpr uint32_t i_ya = umma::idesc_bf16(128, 64, false, true);
@@ -439,6 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     umma::fence_after_sync();
 
+    M3_TC_MARK(13);
     // ---- epilogue: ybar -> dz, dv ---------------------------------------------------------
     {
       float yi[32], ya[32];
@@ -503,6 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
+    M3_TC_MARK(14);
     // ---- pullback through the rotation (fp32, recomputed q~ / k~), 8 pairs at a time -------
     float dsc = 0.f, dAp = 0.f;
     {
@@ -585,6 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (half == 0) reinterpret_cast<float*>(sm + kScrDtb)[t] = dt;
     __syncthreads();
 
+    M3_TC_MARK(15);
     // ---- bias column sums; angle adjoints (suffix over tokens) ------------------------------
     {
       const int n = tid & 127;
@@ -631,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
 
+    M3_TC_MARK(16);
     // ---- per-token scalars: dadt (suffix of dA + the A_last term), preprocess adjoint -------
     {
       const float dscl = part[t] + part[256 + t];
@@ -676,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
+    M3_TC_MARK(17);
     // ---- round 3 result: G <- exp2(A_last) G + dG; A_last term of the previous chunk -------
     if (__syncthreads_or(!umma::mbar_wait(&ss->mbar[2], (nchunk - 1 - c) & 1))) {
       if (tid == 0) atomicExch(&g_m3_device_error, 13);
@@ -705,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
+    M3_TC_MARK(18);
   }
 
   if (ok) {

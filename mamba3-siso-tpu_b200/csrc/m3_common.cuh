@@ -38,6 +38,22 @@ __device__ __forceinline__ float heavy_tail(float x) { return fmaxf(x, 0.f) + 1.
 // phi - 2 pi floor(phi / 2 pi)  (reference.py:156)
 __device__ __forceinline__ float wrap2pi(float x) { return x - kTwoPi * floorf(x / kTwoPi); }
 
+// Packed fp32x2 arithmetic (sm_100 FFMA2 / FADD2 / FMUL2): one instruction per two
+// lanes of work, each component rounded exactly as its scalar counterpart.
+__device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y); }
+__device__ __forceinline__ float2 f2s(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// the two bf16 halves of a packed word as fp32 (exact)
+__device__ __forceinline__ float2 bf2f(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t f2bf(float2 v) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
 // sin / cos of an angle in [0, 2 pi) through the SFU (accurate on [-pi, pi]).
 __device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
   if (x >= kPi) x -= kTwoPi;
@@ -56,11 +72,18 @@ __device__ __forceinline__ float wrap_fast(float x) {
   return x - kTwoPi * floorf(x * 0.15915494309189535f);
 }
 
-// tanh from exp2 and a correctly rounded reciprocal: |error| ~ 1e-7 absolute and
-// unbiased, so the cumulative angle does not drift (tanh.approx's 2^-11 would).
+// 1/x on the SFU (rcp.approx: about 1 ulp; flushes subnormals).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// tanh from exp2 and the SFU reciprocal: |error| ~ 1e-7 absolute and unbiased, so the
+// cumulative angle does not drift (tanh.approx's 2^-11 would).
 __device__ __forceinline__ float tanh_acc(float x) {
   const float e = ex2(2.f * kLog2e * fminf(fabsf(x), 15.f));
-  const float t = 1.f - 2.f * __frcp_rn(e + 1.f);
+  const float t = 1.f - 2.f * rcp_approx(e + 1.f);
   return copysignf(t, x);
 }
 

@@ -170,9 +170,9 @@ int read_device_error(int reset) {
 
 #ifdef M3_TC_TIMING
 extern "C" int m3_debug_tc_timing(unsigned long long* out, int reset) {
-  cudaMemcpyFromSymbol(out, m3::g_m3_tc_timing, sizeof(unsigned long long) * 8);
+  cudaMemcpyFromSymbol(out, m3::g_m3_tc_timing, sizeof(unsigned long long) * 24);
   if (reset) {
-    unsigned long long z[8] = {};
+    unsigned long long z[24] = {};
     cudaMemcpyToSymbol(m3::g_m3_tc_timing, z, sizeof(z));
   }
   return 0;

@@ -32,7 +32,7 @@ __device__ int g_m3_device_error;  // non-zero after a bounded wait gave up
 
 #ifdef M3_TC_TIMING
 // Per-phase cycle totals of slot-thread 0 of every slot (diagnostic builds only).
-__device__ unsigned long long g_m3_tc_timing[8];
+__device__ unsigned long long g_m3_tc_timing[24];
 #define M3_TC_MARK(i)                                                   \
   do {                                                                  \
     if (ltid == 0) {                                                    \
@@ -88,8 +88,25 @@ __device__ __forceinline__ bool slot_any(int slot, bool pred) {
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 
-// z sigmoid(z) for the output gate (bf16 output: the SFU exp and reciprocal suffice).
-__device__ __forceinline__ float silu_fast(float z) { return z * __frcp_rn(1.f + __expf(-z)); }
+// z sigmoid(z) for the output gate of two columns (bf16 output: the SFU exp2 and
+// reciprocal suffice).
+__device__ __forceinline__ float2 silu2(float2 z) {
+  const float2 m = mul2(z, f2s(-kLog2e));
+  const float2 d = add2(f2(ex2(m.x), ex2(m.y)), f2s(1.f));
+  return mul2(z, f2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+
+// 16 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 
 __device__ __forceinline__ uint4 pack8(const float* f) {
   uint4 u;
@@ -292,9 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
 
       // ---- phase 2: cumulative angles and rotation ---------------------------------------
       // Warp g owns rotary pairs (8g .. 8g+7, 64+8g .. 64+8g+7): one 16-byte swizzle chunk
-      // of each q / k half-row.  Lane l owns tokens l + 32 i; the prefix over tokens is a
-      // warp scan per angle and 32-token block, and the carry across chunks stays in
-      // registers (the same value in every lane of the warp).
+      // of each q / k half-row.  Lane l owns the token pairs (2l, 2l+1) + 64 i; the prefix
+      // over tokens is one warp scan of the pair sums per angle and 64-token block, and the
+      // carry across chunks stays in registers (the same value in every lane of the warp).
       {
         const float* dts = reinterpret_cast<const float*>(sm + kVd + kScrDt);
         const float* scls = reinterpret_cast<const float*>(sm + kVd + kScrScl);
@@ -307,82 +324,83 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
 #pragma unroll
         for (int r = 0; r < 8; ++r) off[r] = carry8[r];
 #pragma unroll 1
-        for (int i = 0; i < 4; ++i) {
-          const int tt = lane + 32 * i, tgl = t0 + tt;
-          float ph[8];
+        for (int i = 0; i < 2; ++i) {
+          const int tb = 64 * i + 2 * lane;
+          float ph[2][8];
           if (grot) {
-            const float* pp = RAW ? a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g
-                                  : a.phi + (bh * L + tgl) * Nr + 8 * g;
-            const float4 lo = *reinterpret_cast<const float4*>(pp);
-            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-            ph[0] = lo.x; ph[1] = lo.y; ph[2] = lo.z; ph[3] = lo.w;
-            ph[4] = hi.x; ph[5] = hi.y; ph[6] = hi.z; ph[7] = hi.w;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int tgl = t0 + tb + j;
+              const float* pp = RAW ? a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g
+                                    : a.phi + (bh * L + tgl) * Nr + 8 * g;
+              const float4 lo = *reinterpret_cast<const float4*>(pp);
+              const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+              ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
+              ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
+            }
             if (RAW) {
-              const float w = kPi * dts[tt];
+              const float2 w = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
 #pragma unroll
               for (int r = 0; r < 8; ++r) {
-                const float th = tanh_acc(ph[r]) * w;
-                const float incl = warp_inclusive_scan(th);
-                ph[r] = off[r] + incl;
+                const float x0 = tanh_acc(ph[0][r]) * w.x, x1 = tanh_acc(ph[1][r]) * w.y;
+                const float incl = warp_inclusive_scan(x0 + x1);
+                ph[1][r] = off[r] + incl;
+                ph[0][r] = ph[1][r] - x1;
                 off[r] += __shfl_sync(0xffffffffu, incl, 31);
               }
             }
           }
-          float cs[8], sn[8];
 #pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            cs[r] = 1.f;
-            sn[r] = 0.f;
-            if (grot) sincos_wrapped(wrap_fast(ph[r]), &sn[r], &cs[r]);
-          }
-          const uint32_t soff = umma::sw128_off(tt, g);
-          const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
-          const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
-          const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
-          const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
-          const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
-          const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
-          const float sc = scls[tt];
-          float oq_lo[8], oq_hi[8], ok_lo[8], ok_hi[8];
-          float uw = 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 bql = __ldg(reinterpret_cast<const float2*>(qbp + 2 * e));
-            const float2 bqh = __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
-            const float2 bkl = __ldg(reinterpret_cast<const float2*>(kbp + 2 * e));
-            const float2 bkh = __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
-            const float ulo[2] = {bf16lo(ql[e]) + bql.x, bf16hi(ql[e]) + bql.y};
-            const float uhi[2] = {bf16lo(qh[e]) + bqh.x, bf16hi(qh[e]) + bqh.y};
-            const float wlo[2] = {bf16lo(kl[e]) + bkl.x, bf16hi(kl[e]) + bkl.y};
-            const float whi[2] = {bf16lo(kh[e]) + bkh.x, bf16hi(kh[e]) + bkh.y};
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int r = 2 * e + u;
-              uw += ulo[u] * wlo[u] + uhi[u] * whi[u];
-              oq_lo[r] = ulo[u] * cs[r] - uhi[u] * sn[r];
-              oq_hi[r] = uhi[u] * cs[r] + ulo[u] * sn[r];
-              ok_lo[r] = wlo[u] * cs[r] - whi[u] * sn[r];
-              ok_hi[r] = whi[u] * cs[r] + wlo[u] * sn[r];
-            }
-          }
-          if (tgl == L - 1 && a.final_k) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
-            float* fk = a.final_k + bh * kN + 8 * g;
-#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int tt = tb + j, tgl = t0 + tt;
+            float cs[8], sn[8];
+  #pragma unroll
             for (int r = 0; r < 8; ++r) {
-              fk[r] = ok_lo[r];
-              fk[64 + r] = ok_hi[r];
+              cs[r] = 1.f;
+              sn[r] = 0.f;
+              if (grot) sincos_wrapped(wrap_fast(ph[j][r]), &sn[r], &cs[r]);
             }
+            const uint32_t soff = umma::sw128_off(tt, g);
+            const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
+            const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+            const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
+            const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
+            const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
+            const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
+            const float sc = scls[tt];
+            uint32_t pq_lo[4], pq_hi[4], pk_lo[4], pk_hi[4];
+            float2 uw2 = f2s(0.f);
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
+              const float2 ns2 = f2(-sn[2 * e], -sn[2 * e + 1]);
+              const float2 ulo = add2(bf2f(ql[e]), __ldg(reinterpret_cast<const float2*>(qbp + 2 * e)));
+              const float2 uhi = add2(bf2f(qh[e]), __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e)));
+              const float2 wlo = add2(bf2f(kl[e]), __ldg(reinterpret_cast<const float2*>(kbp + 2 * e)));
+              const float2 whi = add2(bf2f(kh[e]), __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e)));
+              uw2 = fma2(ulo, wlo, uw2);
+              uw2 = fma2(uhi, whi, uw2);
+              pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
+              pq_hi[e] = f2bf(fma2(ulo, s2, mul2(uhi, c2)));
+              const float2 klo = fma2(whi, ns2, mul2(wlo, c2));
+              const float2 khi = fma2(wlo, s2, mul2(whi, c2));
+              if (tgl == L - 1 && a.final_k) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
+                float* fk = a.final_k + bh * kN + 8 * g + 2 * e;
+                fk[0] = klo.x;
+                fk[1] = klo.y;
+                fk[64] = khi.x;
+                fk[65] = khi.y;
+              }
+              pk_lo[e] = f2bf(mul2(klo, f2s(sc)));
+              pk_hi[e] = f2bf(mul2(khi, f2s(sc)));
+            }
+            const float uw = uw2.x + uw2.y;
+            *reinterpret_cast<uint4*>(sm + kQ + soff) = make_uint4(pq_lo[0], pq_lo[1], pq_lo[2], pq_lo[3]);
+            *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = make_uint4(pq_hi[0], pq_hi[1], pq_hi[2], pq_hi[3]);
+            *reinterpret_cast<uint4*>(sm + kK + soff) = make_uint4(pk_lo[0], pk_lo[1], pk_lo[2], pk_lo[3]);
+            *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = make_uint4(pk_hi[0], pk_hi[1], pk_hi[2], pk_hi[3]);
+            uws[g * 128 + tt] = uw;
           }
-#pragma unroll
-          for (int r = 0; r < 8; ++r) {
-            ok_lo[r] *= sc;
-            ok_hi[r] *= sc;
-          }
-          *reinterpret_cast<uint4*>(sm + kQ + soff) = pack8(oq_lo);
-          *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = pack8(oq_hi);
-          *reinterpret_cast<uint4*>(sm + kK + soff) = pack8(ok_lo);
-          *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = pack8(ok_hi);
-          uws[g * 128 + tt] = uw;
         }
         if (RAW)
 #pragma unroll
@@ -413,11 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
           vreg[4 * j + 2] = u.z;
           vreg[4 * j + 3] = u.w;
 
-          uint4 d;
-          d.x = umma::pack_bf16x2(bf16lo(u.x) * e, bf16hi(u.x) * e);
-          d.y = umma::pack_bf16x2(bf16lo(u.y) * e, bf16hi(u.y) * e);
-          d.z = umma::pack_bf16x2(bf16lo(u.z) * e, bf16hi(u.z) * e);
-          d.w = umma::pack_bf16x2(bf16lo(u.w) * e, bf16hi(u.w) * e);
+          const float2 e2 = f2s(e);
+          const uint4 d = make_uint4(f2bf(mul2(bf2f(u.x), e2)), f2bf(mul2(bf2f(u.y), e2)), f2bf(mul2(bf2f(u.z), e2)),
+                                     f2bf(mul2(bf2f(u.w), e2)));
           *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + j)) = d;
         }
       }
@@ -430,16 +446,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
         if (a.chunk_states && c % chunk_sub == 0) {
           const int nc = L / a.dims.chunk, ci = c / chunk_sub;
           const size_t sb = ((bh * nc + ci) * kP) * kN;
-#pragma unroll 8
+#pragma unroll
           for (int i = 0; i < 32; ++i) {
             const size_t o = sb + (size_t)(32 * half + i) * kN + t;
             if (a.chunk_states_dtype == M3_DTYPE_BF16) ((__nv_bfloat16*)a.chunk_states)[o] = __float2bfloat16_rn(sv[i]);
             else ((float*)a.chunk_states)[o] = sv[i];
           }
         }
-        const float eAl = exp2f(Alast);
+        const float2 eAl = f2s(exp2f(Alast));
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[i] *= eAl;
+        for (int i = 0; i < 32; i += 2) {
+          const float2 r = mul2(f2(sv[i], sv[i + 1]), eAl);
+          sv[i] = r.x;
+          sv[i + 1] = r.y;
+        }
         umma::tmem_st32(tm + lane_base + 192 + 32 * half, sv);
         umma::tmem_wait_st();
       }
@@ -514,15 +534,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
           umma::tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            float m[8];
+            uint32_t m[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int s = sb + 8 * j + e;
-              float val = 0.f;
-              if (any && s < t) val = sv[8 * j + e] * ex2(fminf(A - As[s], 0.f));
-              m[e] = val;
+            for (int e = 0; e < 4; ++e) {
+              const int s = sb + 8 * j + 2 * e;
+              const float2 as = *reinterpret_cast<const float2*>(As + s);
+              const float2 d = add2(f2s(A), f2(-as.x, -as.y));
+              float2 val = mul2(f2(sv[8 * j + 2 * e], sv[8 * j + 2 * e + 1]),
+                                f2(ex2(fminf(d.x, 0.f)), ex2(fminf(d.y, 0.f))));
+              if (!(any && s < t)) val.x = 0.f;
+              if (!(any && s + 1 < t)) val.y = 0.f;
+              m[e] = f2bf(val);
             }
-            *reinterpret_cast<uint4*>(sm + kQ + 16384 * half + umma::sw128_off(t, 4 * cb + j)) = pack8(m);
+            *reinterpret_cast<uint4*>(sm + kQ + 16384 * half + umma::sw128_off(t, 4 * cb + j)) =
+                make_uint4(m[0], m[1], m[2], m[3]);
           }
         }
       }
@@ -556,40 +581,40 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
 
       // ---- phase 6: output -----------------------------------------------------------------
       {
-        float yi[32], ya[32];
-        umma::tmem_ld32(tm + lane_base + 128 + 32 * half, yi);
-        umma::tmem_ld32(tm + lane_base + 32 * half, ya);
-        umma::tmem_wait_ld();
-        const float eA = exp2f(A);
-        float o[32];
+        const float2 eA = f2s(exp2f(A)), dg2 = f2s(dg);
+        __nv_bfloat16* yr = y + (size_t)b * a.y_st.b + (size_t)h * a.y_st.h + (size_t)tg * a.y_st.l + 32 * half;
+        if (z) asm volatile("cp.async.wait_group %0;" ::"n"(1) : "memory");  // the z group (committed before q~ / v)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          o[2 * i] = eA * yi[2 * i] + ya[2 * i] + dg * bf16lo(vreg[i]);
-          o[2 * i + 1] = eA * yi[2 * i + 1] + ya[2 * i + 1] + dg * bf16hi(vreg[i]);
-        }
-        if (a.ybar) {
-          float* yb = a.ybar + (bh * L + tg) * kP + 32 * half;
+        for (int hh = 0; hh < 2; ++hh) {  // 16 columns at a time
+          float yi[16], ya[16];
+          tmem_ld16(tm + lane_base + 128 + 32 * half + 16 * hh, yi);
+          tmem_ld16(tm + lane_base + 32 * half + 16 * hh, ya);
+          umma::tmem_wait_ld();
+          float2 o[8];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(yb + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-        }
-        if (z) {
-          // the z group was committed before the q~ / v prefetch: wait for all but that one
-          asm volatile("cp.async.wait_group %0;" ::"n"(1) : "memory");
+          for (int i = 0; i < 8; ++i)
+            o[i] = fma2(dg2, bf2f(vreg[8 * hh + i]), fma2(eA, f2(yi[2 * i], yi[2 * i + 1]), f2(ya[2 * i], ya[2 * i + 1])));
+          if (a.ybar) {
+            float* yb = a.ybar + (bh * L + tg) * kP + 32 * half + 16 * hh;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 u = *reinterpret_cast<const uint4*>(sm + kK + umma::sw128_off(t, 4 * half + j));
+            for (int i = 0; i < 8; i += 2) *reinterpret_cast<float4*>(yb + 2 * i) = make_float4(o[i].x, o[i].y, o[i + 1].x, o[i + 1].y);
+          }
+          uint32_t packed[8];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            uint4 u = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
+            if (z) u = *reinterpret_cast<const uint4*>(sm + kK + umma::sw128_off(t, 4 * half + 2 * hh + j));
             const uint32_t zz[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float z0 = bf16lo(zz[e]), z1 = bf16hi(zz[e]);
-              o[8 * j + 2 * e] *= silu_fast(z0);
-              o[8 * j + 2 * e + 1] *= silu_fast(z1);
+              float2 r = o[4 * j + e];
+              if (z) r = mul2(r, silu2(bf2f(zz[e])));
+              packed[4 * j + e] = f2bf(r);
             }
           }
+          *reinterpret_cast<uint4*>(yr + 16 * hh) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint4*>(yr + 16 * hh + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
-        __nv_bfloat16* yr = y + (size_t)b * a.y_st.b + (size_t)h * a.y_st.h + (size_t)tg * a.y_st.l + 32 * half;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(yr + 8 * j) = pack8(o + 8 * j);
       }
       umma::cp_async_wait_all();  // z reads done and nothing of ours still lands in the khat tile
       umma::fence_before_sync();
@@ -612,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       umma::fence_after_sync();
       umma::tmem_ld32(tm + lane_base + 192 + 32 * half, sv);
       umma::tmem_wait_ld();
-#pragma unroll 8
+#pragma unroll
       for (int i = 0; i < 32; ++i) a.final_ssm[(bh * kP + 32 * half + i) * kN + t] = sv[i];
     }
     if (a.final_v && ltid < kP) {
