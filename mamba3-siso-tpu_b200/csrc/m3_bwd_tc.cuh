@@ -218,14 +218,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float g0 = bf16lo(d4[e]), g1 = bf16hi(d4[e]);
+          float2 g2 = bf2f(d4[e]);
           if (zr) {
-            const float z0 = bf16lo(z4[e]), z1 = bf16hi(z4[e]);
-            g0 *= z0 * sigmoidf_(z0);
-            g1 *= z1 * sigmoidf_(z1);
+            const float2 z2 = bf2f(z4[e]);
+            g2 = mul2(g2, mul2(z2, sigmoid2(z2)));
           }
-          gv[8 * j + 2 * e] = g0;
-          gv[8 * j + 2 * e + 1] = g1;
+          gv[8 * j + 2 * e] = g2.x;
+          gv[8 * j + 2 * e + 1] = g2.y;
         }
       }
       float ge[32];
@@ -242,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     M3_TC_MARK(8);
 
     // ---- P1: cumulative angles (from the recorded carry) and rotation; phi to scratch ----
+    // warp g owns rotary pairs 8g .. 8g+7; lane l the token pairs (2l, 2l+1) + 64 i
     {
       const float* dts = reinterpret_cast<const float*>(sm + kScrDt);
       const float* scls = reinterpret_cast<const float*>(sm + kScrScl);
@@ -254,67 +254,79 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int r = 0; r < 8; ++r) off[r] = grot ? phis[(bh * nchunk + c) * Nr + 8 * g + r] : 0.f;
 #pragma unroll 1
-      for (int i = 0; i < 4; ++i) {
-        const int tt = lane + 32 * i, tgl = t0 + tt;
-        float ph[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int i = 0; i < 2; ++i) {
+        const int tb = 64 * i + 2 * lane;
+        float ph[2][8];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) ph[j][r] = 0.f;
         if (grot) {
-          const float* pp = a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g;
-          const float4 lo = *reinterpret_cast<const float4*>(pp);
-          const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-          const float an[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-          const float w = kPi * dts[tt];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float* pp = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tb + j) * a.ang_st.l + 8 * g;
+            const float4 lo = *reinterpret_cast<const float4*>(pp);
+            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+            ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
+            ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
+          }
+          const float2 w = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
-            const float inc = warp_inclusive_scan(tanh_acc(an[r]) * w);
-            ph[r] = off[r] + inc;
+            const float x0 = tanh_acc(ph[0][r]) * w.x, x1 = tanh_acc(ph[1][r]) * w.y;
+            const float inc = warp_inclusive_scan(x0 + x1);
+            ph[1][r] = off[r] + inc;
+            ph[0][r] = ph[1][r] - x1;
             off[r] += __shfl_sync(0xffffffffu, inc, 31);
           }
-          float* pw = phs + (size_t)tt * 64 + 8 * g;
-          *reinterpret_cast<float4*>(pw) = make_float4(ph[0], ph[1], ph[2], ph[3]);
-          *reinterpret_cast<float4*>(pw + 4) = make_float4(ph[4], ph[5], ph[6], ph[7]);
-        }
-        float cs[8], sn[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          cs[r] = 1.f;
-          sn[r] = 0.f;
-          if (grot) sincos_wrapped(wrap_fast(ph[r]), &sn[r], &cs[r]);
-        }
-        const uint32_t soff = umma::sw128_off(tt, g);
-        const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
-        const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
-        const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
-        const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
-        const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
-        const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
-        const float sc = scls[tt];
-        float oq_lo[8], oq_hi[8], ok_lo[8], ok_hi[8];
-        float uw = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 bql = __ldg(reinterpret_cast<const float2*>(qbp + 2 * e));
-          const float2 bqh = __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
-          const float2 bkl = __ldg(reinterpret_cast<const float2*>(kbp + 2 * e));
-          const float2 bkh = __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
-          const float ulo[2] = {bf16lo(ql[e]) + bql.x, bf16hi(ql[e]) + bql.y};
-          const float uhi[2] = {bf16lo(qh[e]) + bqh.x, bf16hi(qh[e]) + bqh.y};
-          const float wlo[2] = {bf16lo(kl[e]) + bkl.x, bf16hi(kl[e]) + bkl.y};
-          const float whi[2] = {bf16lo(kh[e]) + bkh.x, bf16hi(kh[e]) + bkh.y};
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int r = 2 * e + u;
-            uw += ulo[u] * wlo[u] + uhi[u] * whi[u];
-            oq_lo[r] = ulo[u] * cs[r] - uhi[u] * sn[r];
-            oq_hi[r] = uhi[u] * cs[r] + ulo[u] * sn[r];
-            ok_lo[r] = (wlo[u] * cs[r] - whi[u] * sn[r]) * sc;
-            ok_hi[r] = (whi[u] * cs[r] + wlo[u] * sn[r]) * sc;
+          for (int j = 0; j < 2; ++j) {
+            float* pw = phs + (size_t)(tb + j) * 64 + 8 * g;
+            *reinterpret_cast<float4*>(pw) = make_float4(ph[j][0], ph[j][1], ph[j][2], ph[j][3]);
+            *reinterpret_cast<float4*>(pw + 4) = make_float4(ph[j][4], ph[j][5], ph[j][6], ph[j][7]);
           }
         }
-        *reinterpret_cast<uint4*>(sm + kQ + soff) = pack8(oq_lo);
-        *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = pack8(oq_hi);
-        *reinterpret_cast<uint4*>(sm + kK + soff) = pack8(ok_lo);
-        *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = pack8(ok_hi);
-        uws[g * 128 + tt] = uw;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int tt = tb + j;
+          float cs[8], sn[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            cs[r] = 1.f;
+            sn[r] = 0.f;
+            if (grot) sincos_wrapped(wrap_fast(ph[j][r]), &sn[r], &cs[r]);
+          }
+          const uint32_t soff = umma::sw128_off(tt, g);
+          const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
+          const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+          const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
+          const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
+          const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
+          const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
+          const float2 sc = f2s(scls[tt]);
+          uint32_t pq_lo[4], pq_hi[4], pk_lo[4], pk_hi[4];
+          float2 uw2 = f2s(0.f);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
+            const float2 ns2 = f2(-sn[2 * e], -sn[2 * e + 1]);
+            const float2 ulo = add2(bf2f(ql[e]), __ldg(reinterpret_cast<const float2*>(qbp + 2 * e)));
+            const float2 uhi = add2(bf2f(qh[e]), __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e)));
+            const float2 wlo = add2(bf2f(kl[e]), __ldg(reinterpret_cast<const float2*>(kbp + 2 * e)));
+            const float2 whi = add2(bf2f(kh[e]), __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e)));
+            uw2 = fma2(ulo, wlo, uw2);
+            uw2 = fma2(uhi, whi, uw2);
+            pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
+            pq_hi[e] = f2bf(fma2(ulo, s2, mul2(uhi, c2)));
+            pk_lo[e] = f2bf(mul2(fma2(whi, ns2, mul2(wlo, c2)), sc));
+            pk_hi[e] = f2bf(mul2(fma2(wlo, s2, mul2(whi, c2)), sc));
+          }
+          *reinterpret_cast<uint4*>(sm + kQ + soff) = make_uint4(pq_lo[0], pq_lo[1], pq_lo[2], pq_lo[3]);
+          *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = make_uint4(pq_hi[0], pq_hi[1], pq_hi[2], pq_hi[3]);
+          *reinterpret_cast<uint4*>(sm + kK + soff) = make_uint4(pk_lo[0], pk_lo[1], pk_lo[2], pk_lo[3]);
+          *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = make_uint4(pk_hi[0], pk_hi[1], pk_hi[2], pk_hi[3]);
+          uws[g * 128 + tt] = uw2.x + uw2.y;
+        }
       }
     }
     M3_TC_MARK(9);
@@ -467,16 +479,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           float o[8];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int i = 8 * j + 2 * e + u;
-              const float vv = u ? bf16hi(vreg[4 * j + e]) : bf16lo(vreg[4 * j + e]);
-              const float zz = u ? bf16hi(z4[e]) : bf16lo(z4[e]);
-              const float dd = u ? bf16hi(d4[e]) : bf16lo(d4[e]);
-              const float ybar = eA * yi[i] + ya[i] + dg * vv;
-              const float sg = sigmoidf_(zz);
-              o[2 * e + u] = dd * ybar * sg * (1.f + zz * (1.f - sg));
-            }
+            const int i = 8 * j + 2 * e;
+            const float2 z2 = bf2f(z4[e]);
+            const float2 ybar = fma2(f2s(dg), bf2f(vreg[4 * j + e]), fma2(f2s(eA), f2(yi[i], yi[i + 1]), f2(ya[i], ya[i + 1])));
+            const float2 sg = sigmoid2(z2);
+            const float2 tz = fma2(z2, f2(-sg.x, -sg.y), add2(z2, f2s(1.f)));  // 1 + z (1 - sg)
+            const float2 r = mul2(mul2(bf2f(d4[e]), ybar), mul2(sg, tz));
+            o[2 * e] = r.x;
+            o[2 * e + 1] = r.y;
           }
           *reinterpret_cast<float4*>(dzr + 8 * j) = make_float4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<float4*>(dzr + 8 * j + 4) = make_float4(o[4], o[5], o[6], o[7]);
@@ -525,70 +535,100 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dus = reinterpret_cast<float*>(sm + kDu) + t * 128;
       float* dws = reinterpret_cast<float*>(sm + kDw) + t * 128;
       const bool lastk = (tg == L - 1) && a.dfinal_k;
+      float2 dsc2 = f2s(0.f), dAp2 = f2s(0.f);
 #pragma unroll 1
       for (int sbk = 0; sbk < 4; ++sbk) {
         const int j0 = 32 * half + 8 * sbk;
+        const bool grot = j0 < Nr;  // Nr % 8 == 0: the 8 pairs rotate together or not at all
         float dql[8], dqh[8], dkl[8], dkh[8];
         tmem_ld8(tm + lane_base + 128 + j0, dql);
         tmem_ld8(tm + lane_base + 128 + 64 + j0, dqh);
         tmem_ld8(tm + lane_base + 320 + j0, dkl);
         tmem_ld8(tm + lane_base + 320 + 64 + j0, dkh);
-        umma::tmem_wait_ld();
         const uint4 uq0 = *reinterpret_cast<const uint4*>(qr + j0), uq1 = *reinterpret_cast<const uint4*>(qr + 64 + j0);
         const uint4 uk0 = *reinterpret_cast<const uint4*>(kr + j0), uk1 = *reinterpret_cast<const uint4*>(kr + 64 + j0);
         const uint32_t ql[4] = {uq0.x, uq0.y, uq0.z, uq0.w}, qh[4] = {uq1.x, uq1.y, uq1.z, uq1.w};
         const uint32_t kl[4] = {uk0.x, uk0.y, uk0.z, uk0.w}, kh[4] = {uk1.x, uk1.y, uk1.z, uk1.w};
+        float bq[16], bk[16];  // biases of pairs j0 .. j0+7: [0, 8) low halves, [8, 16) high halves
+        {
+          const float4* qb4 = reinterpret_cast<const float4*>(a.q_bias + h * kN + j0);
+          const float4* kb4 = reinterpret_cast<const float4*>(a.k_bias + h * kN + j0);
+          const float4 v[8] = {__ldg(qb4), __ldg(qb4 + 1), __ldg(qb4 + 16), __ldg(qb4 + 17),
+                               __ldg(kb4), __ldg(kb4 + 1), __ldg(kb4 + 16), __ldg(kb4 + 17)};
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            bq[4 * m] = v[m].x; bq[4 * m + 1] = v[m].y; bq[4 * m + 2] = v[m].z; bq[4 * m + 3] = v[m].w;
+            bk[4 * m] = v[4 + m].x; bk[4 * m + 1] = v[4 + m].y; bk[4 * m + 2] = v[4 + m].z; bk[4 * m + 3] = v[4 + m].w;
+          }
+        }
         float* pp = phs + (size_t)t * 64 + j0;
         float phv[8];
-        {
+        if (grot) {
           const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
           phv[0] = p0.x; phv[1] = p0.y; phv[2] = p0.z; phv[3] = p0.w;
           phv[4] = p1.x; phv[5] = p1.y; phv[6] = p1.z; phv[7] = p1.w;
         }
-        float dul[8], duh[8], dwl[8], dwh[8], dph[8];
+        umma::tmem_wait_ld();
+        float2 dul[4], duh[4], dwl[4], dwh[4], dph[4];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const int j = j0 + r;
-          const float ulo = ((r & 1) ? bf16hi(ql[r >> 1]) : bf16lo(ql[r >> 1])) + a.q_bias[h * kN + j];
-          const float uhi = ((r & 1) ? bf16hi(qh[r >> 1]) : bf16lo(qh[r >> 1])) + a.q_bias[h * kN + 64 + j];
-          const float wlo = ((r & 1) ? bf16hi(kl[r >> 1]) : bf16lo(kl[r >> 1])) + a.k_bias[h * kN + j];
-          const float whi = ((r & 1) ? bf16hi(kh[r >> 1]) : bf16lo(kh[r >> 1])) + a.k_bias[h * kN + 64 + j];
-          float cs = 1.f, sn = 0.f;
-          if (j < Nr) sincos_wrapped(wrap_fast(phv[r]), &sn, &cs);
-          const float qlo = ulo * cs - uhi * sn, qhi = uhi * cs + ulo * sn;
-          const float klo = wlo * cs - whi * sn, khi = whi * cs + wlo * sn;
-          float dklo = dkl[r] * scl, dkhi = dkh[r] * scl;
-          if (lastk) {
-            dklo += a.dfinal_k[bh * kN + j];
-            dkhi += a.dfinal_k[bh * kN + 64 + j];
+        for (int e = 0; e < 4; ++e) {
+          const int r = 2 * e;
+          float2 c2 = f2s(1.f), s2 = f2s(0.f);
+          if (grot) {
+            sincos_wrapped(wrap_fast(phv[r]), &s2.x, &c2.x);
+            sincos_wrapped(wrap_fast(phv[r + 1]), &s2.y, &c2.y);
           }
-          dul[r] = dql[r] * cs + dqh[r] * sn + dgm * wlo;
-          duh[r] = dqh[r] * cs - dql[r] * sn + dgm * whi;
-          dwl[r] = dklo * cs + dkhi * sn + dgm * ulo;
-          dwh[r] = dkhi * cs - dklo * sn + dgm * uhi;
-          dsc += dkl[r] * klo + dkh[r] * khi;
-          dAp += qlo * dql[r] + qhi * dqh[r] - scl * (klo * dkl[r] + khi * dkh[r]);
-          dph[r] = j < Nr ? (dqh[r] * qlo - dql[r] * qhi) + (dkhi * klo - dklo * khi) : 0.f;
+          const float2 ns2 = f2(-s2.x, -s2.y);
+          const float2 ulo = add2(bf2f(ql[e]), f2(bq[r], bq[r + 1]));
+          const float2 uhi = add2(bf2f(qh[e]), f2(bq[8 + r], bq[8 + r + 1]));
+          const float2 wlo = add2(bf2f(kl[e]), f2(bk[r], bk[r + 1]));
+          const float2 whi = add2(bf2f(kh[e]), f2(bk[8 + r], bk[8 + r + 1]));
+          const float2 qlo = fma2(uhi, ns2, mul2(ulo, c2)), qhi = fma2(ulo, s2, mul2(uhi, c2));
+          const float2 klo = fma2(whi, ns2, mul2(wlo, c2)), khi = fma2(wlo, s2, mul2(whi, c2));
+          const float2 gql = f2(dql[r], dql[r + 1]), gqh = f2(dqh[r], dqh[r + 1]);
+          const float2 gkl = f2(dkl[r], dkl[r + 1]), gkh = f2(dkh[r], dkh[r + 1]);
+          float2 dklo = mul2(gkl, f2s(scl)), dkhi = mul2(gkh, f2s(scl));
+          if (lastk) {
+            const float* fk = a.dfinal_k + bh * kN + j0 + r;
+            dklo = add2(dklo, f2(fk[0], fk[1]));
+            dkhi = add2(dkhi, f2(fk[64], fk[65]));
+          }
+          const float2 dg2 = f2s(dgm);
+          dul[e] = fma2(dg2, wlo, fma2(gqh, s2, mul2(gql, c2)));
+          duh[e] = fma2(dg2, whi, fma2(gql, ns2, mul2(gqh, c2)));
+          dwl[e] = fma2(dg2, ulo, fma2(dkhi, s2, mul2(dklo, c2)));
+          dwh[e] = fma2(dg2, uhi, fma2(dklo, ns2, mul2(dkhi, c2)));
+          const float2 kd = fma2(gkh, khi, mul2(gkl, klo));  // khat-side inner product
+          dsc2 = add2(dsc2, kd);
+          dAp2 = fma2(f2s(-scl), kd, fma2(qhi, gqh, fma2(qlo, gql, dAp2)));
+          dph[e] = grot ? add2(fma2(gqh, qlo, mul2(f2(-gql.x, -gql.y), qhi)), fma2(dkhi, klo, mul2(f2(-dklo.x, -dklo.y), khi)))
+                        : f2s(0.f);
         }
-        *reinterpret_cast<float4*>(pp) = make_float4(dph[0], dph[1], dph[2], dph[3]);
-        *reinterpret_cast<float4*>(pp + 4) = make_float4(dph[4], dph[5], dph[6], dph[7]);
-        red_add4(dqrow + j0, dul[0], dul[1], dul[2], dul[3]);
-        red_add4(dqrow + j0 + 4, dul[4], dul[5], dul[6], dul[7]);
-        red_add4(dqrow + 64 + j0, duh[0], duh[1], duh[2], duh[3]);
-        red_add4(dqrow + 64 + j0 + 4, duh[4], duh[5], duh[6], duh[7]);
-        red_add4(dkrow + j0, dwl[0], dwl[1], dwl[2], dwl[3]);
-        red_add4(dkrow + j0 + 4, dwl[4], dwl[5], dwl[6], dwl[7]);
-        red_add4(dkrow + 64 + j0, dwh[0], dwh[1], dwh[2], dwh[3]);
-        red_add4(dkrow + 64 + j0 + 4, dwh[4], dwh[5], dwh[6], dwh[7]);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {  // per-head rows for the bias reductions
-          const int sw = t & 31;
-          dus[(j0 + r) ^ sw] = dul[r];
-          dus[(64 + j0 + r) ^ sw] = duh[r];
-          dws[(j0 + r) ^ sw] = dwl[r];
-          dws[(64 + j0 + r) ^ sw] = dwh[r];
+        if (grot) {
+          *reinterpret_cast<float4*>(pp) = make_float4(dph[0].x, dph[0].y, dph[1].x, dph[1].y);
+          *reinterpret_cast<float4*>(pp + 4) = make_float4(dph[2].x, dph[2].y, dph[3].x, dph[3].y);
         }
+        red_add4(dqrow + j0, dul[0].x, dul[0].y, dul[1].x, dul[1].y);
+        red_add4(dqrow + j0 + 4, dul[2].x, dul[2].y, dul[3].x, dul[3].y);
+        red_add4(dqrow + 64 + j0, duh[0].x, duh[0].y, duh[1].x, duh[1].y);
+        red_add4(dqrow + 64 + j0 + 4, duh[2].x, duh[2].y, duh[3].x, duh[3].y);
+        red_add4(dkrow + j0, dwl[0].x, dwl[0].y, dwl[1].x, dwl[1].y);
+        red_add4(dkrow + j0 + 4, dwl[2].x, dwl[2].y, dwl[3].x, dwl[3].y);
+        red_add4(dkrow + 64 + j0, dwh[0].x, dwh[0].y, dwh[1].x, dwh[1].y);
+        red_add4(dkrow + 64 + j0 + 4, dwh[2].x, dwh[2].y, dwh[3].x, dwh[3].y);
+        // per-head rows for the bias reductions, float4 groups XOR-swizzled by token
+        const int sw = t & 7;
+        *reinterpret_cast<float4*>(dus + 4 * (((j0 >> 2)) ^ sw)) = make_float4(dul[0].x, dul[0].y, dul[1].x, dul[1].y);
+        *reinterpret_cast<float4*>(dus + 4 * (((j0 >> 2) + 1) ^ sw)) = make_float4(dul[2].x, dul[2].y, dul[3].x, dul[3].y);
+        *reinterpret_cast<float4*>(dus + 4 * (((64 + j0) >> 2) ^ sw)) = make_float4(duh[0].x, duh[0].y, duh[1].x, duh[1].y);
+        *reinterpret_cast<float4*>(dus + 4 * ((((64 + j0) >> 2) + 1) ^ sw)) = make_float4(duh[2].x, duh[2].y, duh[3].x, duh[3].y);
+        *reinterpret_cast<float4*>(dws + 4 * (((j0 >> 2)) ^ sw)) = make_float4(dwl[0].x, dwl[0].y, dwl[1].x, dwl[1].y);
+        *reinterpret_cast<float4*>(dws + 4 * (((j0 >> 2) + 1) ^ sw)) = make_float4(dwl[2].x, dwl[2].y, dwl[3].x, dwl[3].y);
+        *reinterpret_cast<float4*>(dws + 4 * (((64 + j0) >> 2) ^ sw)) = make_float4(dwh[0].x, dwh[0].y, dwh[1].x, dwh[1].y);
+        *reinterpret_cast<float4*>(dws + 4 * ((((64 + j0) >> 2) + 1) ^ sw)) = make_float4(dwh[2].x, dwh[2].y, dwh[3].x, dwh[3].y);
       }
+      dsc = dsc2.x + dsc2.y;
+      dAp = dAp2.x + dAp2.y;
     }
     float* part = reinterpret_cast<float*>(sm + kScrPart);  // [2 halves][2][128]: dscale, dA
     part[(half * 2 + 0) * 128 + t] = dsc;
@@ -603,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* src = reinterpret_cast<const float*>(sm + (half ? kDw : kDu));
       float acc = 0.f;
 #pragma unroll 8
-      for (int tt = 0; tt < 128; ++tt) acc += src[tt * 128 + (n ^ (tt & 31))];
+      for (int tt = 0; tt < 128; ++tt) acc += src[tt * 128 + ((((n >> 2) ^ (tt & 7)) << 2) | (n & 3))];
       bias_acc += acc;
     }
     {
@@ -612,33 +652,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dthp = reinterpret_cast<float*>(sm + kScrTh);  // [8][128]
       const float* dts = reinterpret_cast<const float*>(sm + kScrDtb);
 #pragma unroll 1
-      for (int i = 3; i >= 0; --i) {
-        const int tt = lane + 32 * i, tgl = t0 + tt;
-        float share = 0.f;
+      for (int i = 1; i >= 0; --i) {  // lane l: tokens 2l, 2l+1 of the 64-token block i
+        const int tb = 64 * i + 2 * lane;
+        float share[2] = {0.f, 0.f};
         if (grot) {
-          const float* pp = phs + (size_t)tt * 64 + 8 * g;
-          const float4 lo = *reinterpret_cast<const float4*>(pp);
-          const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-          const float dp[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-          const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g;
-          const float4 alo = *reinterpret_cast<const float4*>(ap);
-          const float4 ahi = *reinterpret_cast<const float4*>(ap + 4);
-          const float an[8] = {alo.x, alo.y, alo.z, alo.w, ahi.x, ahi.y, ahi.z, ahi.w};
-          float dan[8];
+          float dp[2][8], an[2][8];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float* pp = phs + (size_t)(tb + j) * 64 + 8 * g;
+            const float4 lo = *reinterpret_cast<const float4*>(pp);
+            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+            dp[j][0] = lo.x; dp[j][1] = lo.y; dp[j][2] = lo.z; dp[j][3] = lo.w;
+            dp[j][4] = hi.x; dp[j][5] = hi.y; dp[j][6] = hi.z; dp[j][7] = hi.w;
+            const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tb + j) * a.ang_st.l + 8 * g;
+            const float4 alo = *reinterpret_cast<const float4*>(ap);
+            const float4 ahi = *reinterpret_cast<const float4*>(ap + 4);
+            an[j][0] = alo.x; an[j][1] = alo.y; an[j][2] = alo.z; an[j][3] = alo.w;
+            an[j][4] = ahi.x; an[j][5] = ahi.y; an[j][6] = ahi.z; an[j][7] = ahi.w;
+          }
+          const float2 wdt = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
+          float dan[2][8];
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
-            const float sfx = warp_suffix_scan(dp[r]);
-            const float dth = dcarry8[r] + sfx;
+            // suffix over tokens: this lane's pair plus every later lane of the block
+            const float sfx = warp_suffix_scan(dp[0][r] + dp[1][r]);
+            const float dth0 = dcarry8[r] + sfx, dth1 = dth0 - dp[0][r];
             dcarry8[r] += __shfl_sync(0xffffffffu, sfx, 0);
-            const float th = tanh_acc(an[r]);
-            dan[r] = dth * kPi * dts[tt] * (1.f - th * th);
-            share += dth * th * kPi;
+            const float th0 = tanh_acc(an[0][r]), th1 = tanh_acc(an[1][r]);
+            dan[0][r] = dth0 * wdt.x * (1.f - th0 * th0);
+            dan[1][r] = dth1 * wdt.y * (1.f - th1 * th1);
+            share[0] += dth0 * th0 * kPi;
+            share[1] += dth1 * th1 * kPi;
           }
-          float* dap = a.dangles + ((size_t)b * L + tgl) * Nr + 8 * g;
-          red_add4(dap, dan[0], dan[1], dan[2], dan[3]);
-          red_add4(dap + 4, dan[4], dan[5], dan[6], dan[7]);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float* dap = a.dangles + ((size_t)b * L + t0 + tb + j) * Nr + 8 * g;
+            red_add4(dap, dan[j][0], dan[j][1], dan[j][2], dan[j][3]);
+            red_add4(dap + 4, dan[j][4], dan[j][5], dan[j][6], dan[j][7]);
+          }
         }
-        dthp[g * 128 + tt] = share;
+        *reinterpret_cast<float2*>(dthp + g * 128 + tb) = f2(share[0], share[1]);
       }
     }
     __syncthreads();

@@ -87,6 +87,15 @@ __device__ __forceinline__ float tanh_acc(float x) {
   return copysignf(t, x);
 }
 
+// sigmoid of two values on the SFU (exp2 and reciprocal; ~1e-7 relative), for the
+// bf16-output gate of the tensor-core kernels.
+__device__ __forceinline__ float2 sigmoid2(float2 z) {
+  const float2 m = mul2(z, f2s(-kLog2e));
+  const float2 d = add2(f2(ex2(m.x), ex2(m.y)), f2s(1.f));
+  return f2(rcp_approx(d.x), rcp_approx(d.y));
+}
+__device__ __forceinline__ float2 silu2(float2 z) { return mul2(z, sigmoid2(z)); }
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);

@@ -88,14 +88,6 @@ __device__ __forceinline__ bool slot_any(int slot, bool pred) {
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t u) { return __uint_as_float(u & 0xFFFF0000u); }
 
-// z sigmoid(z) for the output gate of two columns (bf16 output: the SFU exp2 and
-// reciprocal suffice).
-__device__ __forceinline__ float2 silu2(float2 z) {
-  const float2 m = mul2(z, f2s(-kLog2e));
-  const float2 d = add2(f2(ex2(m.x), ex2(m.y)), f2s(1.f));
-  return mul2(z, f2(rcp_approx(d.x), rcp_approx(d.y)));
-}
-
 // 16 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
