@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < 4; ++j)
       *reinterpret_cast<uint4*>(sm + kGt + umma::sw128_off(t, 4 * half + j)) = pack8(G + 8 * j);
   }
-  float bias_acc = 0.f, dD_acc = 0.f, ddtb_acc = 0.f;
+  float2 bias01 = f2s(0.f), bias23 = f2s(0.f);  // bias column sums (see the row pass)
+  float dD_acc = 0.f, ddtb_acc = 0.f;
   __syncthreads();
 
 #ifdef M3_TC_TIMING
@@ -453,6 +454,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma::commit(&ss->mbar[1]);
     }
+    // dy / z rows for the dz epilogue: loads in flight while round 2 runs
+    uint4 ud[4], uz[4];
+    {
+      const __nv_bfloat16* dyr = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tg * a.dy_st.l + 32 * half;
+      const __nv_bfloat16* zr = z ? z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half
+                                  : nullptr;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ud[j] = *reinterpret_cast<const uint4*>(dyr + 8 * j);
+        uz[j] = zr ? *reinterpret_cast<const uint4*>(zr + 8 * j) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
     if (__syncthreads_or(!umma::mbar_wait(&ss->mbar[1], (nchunk - 1 - c) & 1))) {
       if (tid == 0) atomicExch(&g_m3_device_error, 12);
       ok = false;
@@ -462,32 +475,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     M3_TC_MARK(13);
     // ---- epilogue: ybar -> dz, dv ---------------------------------------------------------
+    float gq[32];  // g = dy silu(z) once more (same arithmetic as above) for dv's diagonal term
     {
       float yi[32], ya[32];
       umma::tmem_ld32(tm + lane_base + 256 + 32 * half, yi);
       umma::tmem_ld32(tm + lane_base + 32 * half, ya);
       umma::tmem_wait_ld();
-      if (z) {
-        const __nv_bfloat16* dyr = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tg * a.dy_st.l + 32 * half;
-        const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
-        float* dzr = a.dz + (bh * L + tg) * kP + 32 * half;
+      float* dzr = z ? a.dz + (bh * L + tg) * kP + 32 * half : nullptr;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 ud = *reinterpret_cast<const uint4*>(dyr + 8 * j);
-          const uint4 uz = *reinterpret_cast<const uint4*>(zr + 8 * j);
-          const uint32_t d4[4] = {ud.x, ud.y, ud.z, ud.w}, z4[4] = {uz.x, uz.y, uz.z, uz.w};
-          float o[8];
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t d4[4] = {ud[j].x, ud[j].y, ud[j].z, ud[j].w}, z4[4] = {uz[j].x, uz[j].y, uz[j].z, uz[j].w};
+        float o[8];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 8 * j + 2 * e;
+        for (int e = 0; e < 4; ++e) {
+          const int i = 8 * j + 2 * e;
+          const float2 d2 = bf2f(d4[e]);
+          float2 g2 = d2;
+          if (z) {
             const float2 z2 = bf2f(z4[e]);
-            const float2 ybar = fma2(f2s(dg), bf2f(vreg[4 * j + e]), fma2(f2s(eA), f2(yi[i], yi[i + 1]), f2(ya[i], ya[i + 1])));
             const float2 sg = sigmoid2(z2);
+            g2 = mul2(d2, mul2(z2, sg));
+            const float2 ybar = fma2(f2s(dg), bf2f(vreg[4 * j + e]), fma2(f2s(eA), f2(yi[i], yi[i + 1]), f2(ya[i], ya[i + 1])));
             const float2 tz = fma2(z2, f2(-sg.x, -sg.y), add2(z2, f2s(1.f)));  // 1 + z (1 - sg)
-            const float2 r = mul2(mul2(bf2f(d4[e]), ybar), mul2(sg, tz));
+            const float2 r = mul2(mul2(d2, ybar), mul2(sg, tz));
             o[2 * e] = r.x;
             o[2 * e + 1] = r.y;
           }
+          gq[i] = g2.x;
+          gq[i + 1] = g2.y;
+        }
+        if (z) {
           *reinterpret_cast<float4*>(dzr + 8 * j) = make_float4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<float4*>(dzr + 8 * j + 4) = make_float4(o[4], o[5], o[6], o[7]);
         }
@@ -516,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float o[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          o[u] = da[i + u] + erev * db[i + u] + dg * gv[i + u];
+          o[u] = da[i + u] + erev * db[i + u] + dg * gq[i + u];
           if (last) o[u] += a.dfinal_v[bh * kP + 32 * half + i + u];
         }
         *reinterpret_cast<float4*>(dvr + i) = make_float4(o[0], o[1], o[2], o[3]);
@@ -530,13 +547,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tg * a.q_st.l;
       const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tg * a.k_st.l;
       const float dgm = qkd * gam;
-      float* dqrow = a.dq + ((size_t)b * L + tg) * kN;
-      float* dkrow = a.dk + ((size_t)b * L + tg) * kN;
       float* dus = reinterpret_cast<float*>(sm + kDu) + t * 128;
       float* dws = reinterpret_cast<float*>(sm + kDw) + t * 128;
       const bool lastk = (tg == L - 1) && a.dfinal_k;
       float2 dsc2 = f2s(0.f), dAp2 = f2s(0.f);
-#pragma unroll 1
+#pragma unroll 2
       for (int sbk = 0; sbk < 4; ++sbk) {
         const int j0 = 32 * half + 8 * sbk;
         const bool grot = j0 < Nr;  // Nr % 8 == 0: the 8 pairs rotate together or not at all
@@ -608,14 +623,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(pp) = make_float4(dph[0].x, dph[0].y, dph[1].x, dph[1].y);
           *reinterpret_cast<float4*>(pp + 4) = make_float4(dph[2].x, dph[2].y, dph[3].x, dph[3].y);
         }
-        red_add4(dqrow + j0, dul[0].x, dul[0].y, dul[1].x, dul[1].y);
-        red_add4(dqrow + j0 + 4, dul[2].x, dul[2].y, dul[3].x, dul[3].y);
-        red_add4(dqrow + 64 + j0, duh[0].x, duh[0].y, duh[1].x, duh[1].y);
-        red_add4(dqrow + 64 + j0 + 4, duh[2].x, duh[2].y, duh[3].x, duh[3].y);
-        red_add4(dkrow + j0, dwl[0].x, dwl[0].y, dwl[1].x, dwl[1].y);
-        red_add4(dkrow + j0 + 4, dwl[2].x, dwl[2].y, dwl[3].x, dwl[3].y);
-        red_add4(dkrow + 64 + j0, dwh[0].x, dwh[0].y, dwh[1].x, dwh[1].y);
-        red_add4(dkrow + 64 + j0 + 4, dwh[2].x, dwh[2].y, dwh[3].x, dwh[3].y);
         // per-head rows for the bias reductions, float4 groups XOR-swizzled by token
         const int sw = t & 7;
         *reinterpret_cast<float4*>(dus + 4 * (((j0 >> 2)) ^ sw)) = make_float4(dul[0].x, dul[0].y, dul[1].x, dul[1].y);
@@ -639,12 +646,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     M3_TC_MARK(15);
     // ---- bias column sums; angle adjoints (suffix over tokens) ------------------------------
     {
-      const int n = tid & 127;
-      const float* src = reinterpret_cast<const float*>(sm + (half ? kDw : kDu));
-      float acc = 0.f;
-#pragma unroll 8
-      for (int tt = 0; tt < 128; ++tt) acc += src[tt * 128 + ((((n >> 2) ^ (tt & 7)) << 2) | (n & 3))];
-      bias_acc += acc;
+      // warps 0-3: du rows (-> dq), warps 4-7: dw rows (-> dk), 32 token rows each; lane l
+      // owns columns 4l .. 4l+3.  Row-contiguous head-sum adds (one 512-byte row per warp
+      // instruction) and the per-head bias column sums from the same loads.
+      const int mat = warp >> 2;
+      const float* src = reinterpret_cast<const float*>(sm + (mat ? kDw : kDu));
+      float* dst = (mat ? a.dk : a.dq) + ((size_t)b * L + t0) * kN + 4 * lane;
+#pragma unroll 4
+      for (int rr = 0; rr < 32; ++rr) {
+        const int tt = 32 * (warp & 3) + rr;
+        const float4 v = *reinterpret_cast<const float4*>(src + tt * 128 + 4 * (lane ^ (tt & 7)));
+        bias01 = add2(bias01, f2(v.x, v.y));
+        bias23 = add2(bias23, f2(v.z, v.w));
+        red_add4(dst + (size_t)tt * kN, v.x, v.y, v.z, v.w);
+      }
     }
     {
       const int g = warp;
@@ -806,7 +821,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (a.dseed_phi && lane == 0 && 8 * warp < Nr)
 #pragma unroll
       for (int r = 0; r < 8; ++r) a.dseed_phi[bh * Nr + 8 * warp + r] = dcarry8[r];
-    atomicAdd((half ? a.dk_bias : a.dq_bias) + h * kN + t, bias_acc);
+    {
+      float* bb = (warp >= 4 ? a.dk_bias : a.dq_bias) + h * kN + 4 * lane;
+      atomicAdd(bb, bias01.x);
+      atomicAdd(bb + 1, bias01.y);
+      atomicAdd(bb + 2, bias23.x);
+      atomicAdd(bb + 3, bias23.y);
+    }
     const float dD = cta_sum(dD_acc, ss);
     const float ddb = cta_sum(ddtb_acc, ss);
     if (tid == 0) {
