@@ -38,6 +38,7 @@ constexpr uint32_t kQ = 0, kGe = 32768, kSt = 49152, kGt = 65536, kK = 81920, kW
 // scratch inside tiles while they are not live
 constexpr uint32_t kScrDt = kWm, kScrScl = kWm + 512, kScrUw = kWm + 1024, kScrQkd = kWm + 5120;   // prep
 constexpr uint32_t kScrPart = kGt, kScrDtb = kGt + 2048, kScrTh = kGt + 2560;                     // epilogue
+constexpr uint32_t kStDv = kDM, kStDz = kV;  // dv / dz rows [128][64] fp32 on their way out (after round 2)
 constexpr uint32_t kDu = kK, kDw = kDM;  // fp32 [128][128] each, column index XOR-swizzled by row
 
 struct Small {
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const __nv_bfloat16* dy = (const __nv_bfloat16*)a.dy;
   const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
   const float dtb = a.dt_bias[h];
-  float* phs = scratch + (size_t)blockIdx.x * (kC * 64);  // [t][64]: phi, then dphi
+  float* phs = scratch + (size_t)blockIdx.x * (kC * 64);  // [64 angles][128 tokens]: phi, then dphi
 
   if (warp == 0) umma::tmem_alloc(&ss->tmem, 512);
   if (tid == 0) {
@@ -281,11 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             off[r] += __shfl_sync(0xffffffffu, inc, 31);
           }
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            float* pw = phs + (size_t)(tb + j) * 64 + 8 * g;
-            *reinterpret_cast<float4*>(pw) = make_float4(ph[j][0], ph[j][1], ph[j][2], ph[j][3]);
-            *reinterpret_cast<float4*>(pw + 4) = make_float4(ph[j][4], ph[j][5], ph[j][6], ph[j][7]);
-          }
+          for (int r = 0; r < 8; ++r)
+            *reinterpret_cast<float2*>(phs + (8 * g + r) * kC + tb) = f2(ph[0][r], ph[1][r]);
         }
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -481,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::tmem_ld32(tm + lane_base + 256 + 32 * half, yi);
       umma::tmem_ld32(tm + lane_base + 32 * half, ya);
       umma::tmem_wait_ld();
-      float* dzr = z ? a.dz + (bh * L + tg) * kP + 32 * half : nullptr;
+      float* dzs = reinterpret_cast<float*>(sm + kStDz) + t * 64;  // float4 groups XOR-swizzled by row
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t d4[4] = {ud[j].x, ud[j].y, ud[j].z, ud[j].w}, z4[4] = {uz[j].x, uz[j].y, uz[j].z, uz[j].w};
@@ -505,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           gq[i + 1] = g2.y;
         }
         if (z) {
-          *reinterpret_cast<float4*>(dzr + 8 * j) = make_float4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<float4*>(dzr + 8 * j + 4) = make_float4(o[4], o[5], o[6], o[7]);
+          *reinterpret_cast<float4*>(dzs + 4 * ((8 * half + 2 * j) ^ (t & 7))) = make_float4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<float4*>(dzs + 4 * ((8 * half + 2 * j + 1) ^ (t & 7))) = make_float4(o[4], o[5], o[6], o[7]);
         }
       }
     }
@@ -526,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::tmem_ld32(tm + lane_base + 64 + 32 * half, da);
       umma::tmem_ld32(tm + lane_base + 448 + 32 * half, db);
       umma::tmem_wait_ld();
-      float* dvr = a.dv + (bh * L + tg) * kP + 32 * half;
+      float* dvs = reinterpret_cast<float*>(sm + kStDv) + t * 64;
       const bool last = (tg == L - 1) && a.dfinal_v;
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
@@ -536,9 +534,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           o[u] = da[i + u] + erev * db[i + u] + dg * gq[i + u];
           if (last) o[u] += a.dfinal_v[bh * kP + 32 * half + i + u];
         }
-        *reinterpret_cast<float4*>(dvr + i) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(dvs + 4 * ((8 * half + i / 4) ^ (t & 7))) = make_float4(o[0], o[1], o[2], o[3]);
       }
     }
+    __syncthreads();
+    {
+      // the chunk's dv (and dz) rows are one contiguous 32 KB block each: coalesced stores
+      const float* dvs = reinterpret_cast<const float*>(sm + kStDv);
+      const float* dzs = reinterpret_cast<const float*>(sm + kStDz);
+      float* dvo = a.dv + (bh * L + t0) * kP;
+      float* dzo = z ? a.dz + (bh * L + t0) * kP : nullptr;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int idx = tid + kThreads * m, row = idx >> 4, g4 = idx & 15;
+        const int so = row * 64 + 4 * (g4 ^ (row & 7));
+        *reinterpret_cast<float4*>(dvo + 4 * idx) = *reinterpret_cast<const float4*>(dvs + so);
+        if (z) *reinterpret_cast<float4*>(dzo + 4 * idx) = *reinterpret_cast<const float4*>(dzs + so);
+      }
+    }
+    __syncthreads();  // the staging tiles are free for the pullback's rows
 
     M3_TC_MARK(14);
     // ---- pullback through the rotation (fp32, recomputed q~ / k~), 8 pairs at a time -------
@@ -576,13 +590,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             bk[4 * m] = v[4 + m].x; bk[4 * m + 1] = v[4 + m].y; bk[4 * m + 2] = v[4 + m].z; bk[4 * m + 3] = v[4 + m].w;
           }
         }
-        float* pp = phs + (size_t)t * 64 + j0;
+        float* pp = phs + j0 * kC + t;
         float phv[8];
-        if (grot) {
-          const float4 p0 = *reinterpret_cast<const float4*>(pp), p1 = *reinterpret_cast<const float4*>(pp + 4);
-          phv[0] = p0.x; phv[1] = p0.y; phv[2] = p0.z; phv[3] = p0.w;
-          phv[4] = p1.x; phv[5] = p1.y; phv[6] = p1.z; phv[7] = p1.w;
-        }
+        if (grot)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) phv[r] = pp[r * kC];
         umma::tmem_wait_ld();
         float2 dul[4], duh[4], dwl[4], dwh[4], dph[4];
 #pragma unroll
@@ -619,10 +631,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           dph[e] = grot ? add2(fma2(gqh, qlo, mul2(f2(-gql.x, -gql.y), qhi)), fma2(dkhi, klo, mul2(f2(-dklo.x, -dklo.y), khi)))
                         : f2s(0.f);
         }
-        if (grot) {
-          *reinterpret_cast<float4*>(pp) = make_float4(dph[0].x, dph[0].y, dph[1].x, dph[1].y);
-          *reinterpret_cast<float4*>(pp + 4) = make_float4(dph[2].x, dph[2].y, dph[3].x, dph[3].y);
-        }
+        if (grot)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            pp[(2 * e) * kC] = dph[e].x;
+            pp[(2 * e + 1) * kC] = dph[e].y;
+          }
         // per-head rows for the bias reductions, float4 groups XOR-swizzled by token
         const int sw = t & 7;
         *reinterpret_cast<float4*>(dus + 4 * (((j0 >> 2)) ^ sw)) = make_float4(dul[0].x, dul[0].y, dul[1].x, dul[1].y);
@@ -673,12 +687,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (grot) {
           float dp[2][8], an[2][8];
 #pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            const float2 d2 = *reinterpret_cast<const float2*>(phs + (8 * g + r) * kC + tb);
+            dp[0][r] = d2.x;
+            dp[1][r] = d2.y;
+          }
+#pragma unroll
           for (int j = 0; j < 2; ++j) {
-            const float* pp = phs + (size_t)(tb + j) * 64 + 8 * g;
-            const float4 lo = *reinterpret_cast<const float4*>(pp);
-            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-            dp[j][0] = lo.x; dp[j][1] = lo.y; dp[j][2] = lo.z; dp[j][3] = lo.w;
-            dp[j][4] = hi.x; dp[j][5] = hi.y; dp[j][6] = hi.z; dp[j][7] = hi.w;
             const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tb + j) * a.ang_st.l + 8 * g;
             const float4 alo = *reinterpret_cast<const float4*>(ap);
             const float4 ahi = *reinterpret_cast<const float4*>(ap + 4);
