@@ -38,8 +38,13 @@ constexpr uint32_t kQ = 0, kGe = 32768, kSt = 49152, kGt = 65536, kK = 81920, kW
 // scratch inside tiles while they are not live
 constexpr uint32_t kScrDt = kWm, kScrScl = kWm + 512, kScrUw = kWm + 1024, kScrQkd = kWm + 5120;   // prep
 constexpr uint32_t kScrPart = kGt, kScrDtb = kGt + 2048, kScrTh = kGt + 2560;                     // epilogue
+constexpr uint32_t kAng = kDM;  // this chunk's raw angles [128][64] fp32, 16-byte chunks XOR-swizzled by row (P0-P1)
 constexpr uint32_t kStDv = kDM, kStDz = kV;  // dv / dz rows [128][64] fp32 on their way out (after round 2)
 constexpr uint32_t kDu = kK, kDw = kDM;  // fp32 [128][128] each, column index XOR-swizzled by row
+
+// per-sequence global scratch: phi then dphi [64][128] fp32, tanh(angles) [64][128] fp32,
+// raw q and k rows as 16-byte column groups [16][128] (all token-contiguous, so coalesced)
+constexpr size_t kScratchBytes = 2 * 64 * kC * sizeof(float) + 2 * 16 * kC * 16;
 
 struct Small {
   uint64_t mbar[3];
@@ -109,7 +114,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const __nv_bfloat16* dy = (const __nv_bfloat16*)a.dy;
   const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
   const float dtb = a.dt_bias[h];
-  float* phs = scratch + (size_t)blockIdx.x * (kC * 64);  // [64 angles][128 tokens]: phi, then dphi
+  float* phs = scratch + (size_t)blockIdx.x * (kScratchBytes / sizeof(float));  // [64][128]: phi, then dphi
+  float* ths = phs + 64 * kC;                                                     // [64][128]: tanh(angles)
+  uint4* rqs = reinterpret_cast<uint4*>(ths + 64 * kC);                            // [16][128]: raw q
+  uint4* rks = rqs + 16 * kC;                                                      // [16][128]: raw k
 
   if (warp == 0) umma::tmem_alloc(&ss->tmem, 512);
   if (tid == 0) {
@@ -178,6 +186,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::cp_async16(aV + umma::sw128_off(row, c8),
                        v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(t0 + row) * a.v_st.l + c8 * 8);
       umma::cp_async16(aSt + 16u * i, tiles + (bh * (nchunk + 1) + c) * 16384u + 16u * i);
+    }
+    {
+      const int n4 = Nr >> 2;  // 16-byte chunks per angle row
+      const uint32_t aAng = umma::smem_u32(sm + kAng);
+      for (int i = tid; i < kC * n4; i += kThreads) {
+        const int row = i / n4, c4 = i - row * n4;
+        umma::cp_async16(aAng + row * 256 + 16 * (c4 ^ (row & 15)),
+                         a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + row) * a.ang_st.l + 4 * c4);
+      }
     }
     umma::cp_async_commit();
     const size_t ro = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
@@ -266,16 +283,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (grot) {
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
-            const float* pp = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tb + j) * a.ang_st.l + 8 * g;
-            const float4 lo = *reinterpret_cast<const float4*>(pp);
-            const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-            ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
-            ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
+            const int row = tb + j;
+            const uint8_t* ap = sm + kAng + row * 256;
+            const float4 lo = *reinterpret_cast<const float4*>(ap + 16 * ((2 * g) ^ (row & 15)));
+            const float4 hi = *reinterpret_cast<const float4*>(ap + 16 * ((2 * g + 1) ^ (row & 15)));
+            ph[j][0] = tanh_acc(lo.x); ph[j][1] = tanh_acc(lo.y); ph[j][2] = tanh_acc(lo.z); ph[j][3] = tanh_acc(lo.w);
+            ph[j][4] = tanh_acc(hi.x); ph[j][5] = tanh_acc(hi.y); ph[j][6] = tanh_acc(hi.z); ph[j][7] = tanh_acc(hi.w);
           }
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            *reinterpret_cast<float2*>(ths + (8 * g + r) * kC + tb) = f2(ph[0][r], ph[1][r]);
           const float2 w = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
-            const float x0 = tanh_acc(ph[0][r]) * w.x, x1 = tanh_acc(ph[1][r]) * w.y;
+            const float x0 = ph[0][r] * w.x, x1 = ph[1][r] * w.y;
             const float inc = warp_inclusive_scan(x0 + x1);
             ph[1][r] = off[r] + inc;
             ph[0][r] = ph[1][r] - x1;
@@ -300,6 +321,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
           const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
           const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
+          rqs[g * kC + tt] = uql;  // raw rows for the pullback
+          rqs[(8 + g) * kC + tt] = uqh;
+          rks[g * kC + tt] = ukl;
+          rks[(8 + g) * kC + tt] = ukh;
           const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
           const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
           const float2 sc = f2s(scls[tt]);
@@ -558,8 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- pullback through the rotation (fp32, recomputed q~ / k~), 8 pairs at a time -------
     float dsc = 0.f, dAp = 0.f;
     {
-      const __nv_bfloat16* qr = q + (size_t)b * a.q_st.b + (size_t)tg * a.q_st.l;
-      const __nv_bfloat16* kr = k + (size_t)b * a.k_st.b + (size_t)tg * a.k_st.l;
       const float dgm = qkd * gam;
       float* dus = reinterpret_cast<float*>(sm + kDu) + t * 128;
       float* dws = reinterpret_cast<float*>(sm + kDw) + t * 128;
@@ -574,8 +597,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld8(tm + lane_base + 128 + 64 + j0, dqh);
         tmem_ld8(tm + lane_base + 320 + j0, dkl);
         tmem_ld8(tm + lane_base + 320 + 64 + j0, dkh);
-        const uint4 uq0 = *reinterpret_cast<const uint4*>(qr + j0), uq1 = *reinterpret_cast<const uint4*>(qr + 64 + j0);
-        const uint4 uk0 = *reinterpret_cast<const uint4*>(kr + j0), uk1 = *reinterpret_cast<const uint4*>(kr + 64 + j0);
+        const uint4 uq0 = rqs[(j0 >> 3) * kC + t], uq1 = rqs[(8 + (j0 >> 3)) * kC + t];
+        const uint4 uk0 = rks[(j0 >> 3) * kC + t], uk1 = rks[(8 + (j0 >> 3)) * kC + t];
         const uint32_t ql[4] = {uq0.x, uq0.y, uq0.z, uq0.w}, qh[4] = {uq1.x, uq1.y, uq1.z, uq1.w};
         const uint32_t kl[4] = {uk0.x, uk0.y, uk0.z, uk0.w}, kh[4] = {uk1.x, uk1.y, uk1.z, uk1.w};
         float bq[16], bk[16];  // biases of pairs j0 .. j0+7: [0, 8) low halves, [8, 16) high halves
@@ -685,20 +708,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tb = 64 * i + 2 * lane;
         float share[2] = {0.f, 0.f};
         if (grot) {
-          float dp[2][8], an[2][8];
+          float dp[2][8], th[2][8];
 #pragma unroll
           for (int r = 0; r < 8; ++r) {
             const float2 d2 = *reinterpret_cast<const float2*>(phs + (8 * g + r) * kC + tb);
+            const float2 t2 = *reinterpret_cast<const float2*>(ths + (8 * g + r) * kC + tb);
             dp[0][r] = d2.x;
             dp[1][r] = d2.y;
-          }
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const float* ap = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tb + j) * a.ang_st.l + 8 * g;
-            const float4 alo = *reinterpret_cast<const float4*>(ap);
-            const float4 ahi = *reinterpret_cast<const float4*>(ap + 4);
-            an[j][0] = alo.x; an[j][1] = alo.y; an[j][2] = alo.z; an[j][3] = alo.w;
-            an[j][4] = ahi.x; an[j][5] = ahi.y; an[j][6] = ahi.z; an[j][7] = ahi.w;
+            th[0][r] = t2.x;
+            th[1][r] = t2.y;
           }
           const float2 wdt = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
           float dan[2][8];
@@ -708,7 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sfx = warp_suffix_scan(dp[0][r] + dp[1][r]);
             const float dth0 = dcarry8[r] + sfx, dth1 = dth0 - dp[0][r];
             dcarry8[r] += __shfl_sync(0xffffffffu, sfx, 0);
-            const float th0 = tanh_acc(an[0][r]), th1 = tanh_acc(an[1][r]);
+            const float th0 = th[0][r], th1 = th[1][r];
             dan[0][r] = dth0 * wdt.x * (1.f - th0 * th0);
             dan[1][r] = dth1 * wdt.y * (1.f - th1 * th1);
             share[0] += dth0 * th0 * kPi;

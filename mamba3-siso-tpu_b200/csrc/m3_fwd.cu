@@ -95,7 +95,7 @@ static size_t tc_phis_bytes(const M3Dims& d) {
   return (size_t)d.batch * d.nheads * (d.seqlen / tc::kC) * d.n_angles * sizeof(float);
 }
 size_t bwd_tc_workspace_bytes(const M3Dims& d) {
-  return tc_tiles_bytes(d) + tc_phis_bytes(d) + (size_t)d.batch * d.nheads * tcb::kC * 64 * sizeof(float) + 256;
+  return tc_tiles_bytes(d) + tc_phis_bytes(d) + (size_t)d.batch * d.nheads * tcb::kScratchBytes + 256;
 }
 
 bool bwd_tc_eligible(const M3BwdArgs& a) {
