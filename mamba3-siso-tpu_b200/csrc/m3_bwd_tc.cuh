@@ -163,6 +163,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   float dD_acc = 0.f, ddtb_acc = 0.f;
   __syncthreads();
 
+  // Raw tiles of chunk cc (cp.async).  k, v and the angles go to tiles that are free once the
+  // previous chunk's head-sum pass has read its rows; q and the state tile once its round 3
+  // and A_last term are done.
+  auto prefetch_kva = [&](int cc) {
+    const int tb = cc * kC;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 4, c16 = i & 15;
+      const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
+      umma::cp_async16(aK + dst, k + (size_t)b * a.k_st.b + (size_t)(tb + row) * a.k_st.l + c16 * 8);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 3, c8 = i & 7;
+      umma::cp_async16(aV + umma::sw128_off(row, c8),
+                       v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(tb + row) * a.v_st.l + c8 * 8);
+    }
+    const int n4 = Nr >> 2;  // 16-byte chunks per angle row
+    const uint32_t aAng = umma::smem_u32(sm + kAng);
+    for (int i = tid; i < kC * n4; i += kThreads) {
+      const int row = i / n4, c4 = i - row * n4;
+      umma::cp_async16(aAng + row * 256 + 16 * (c4 ^ (row & 15)),
+                       a.angles + (size_t)b * a.ang_st.b + (size_t)(tb + row) * a.ang_st.l + 4 * c4);
+    }
+    umma::cp_async_commit();
+  };
+  auto prefetch_qst = [&](int cc) {
+    const int tb = cc * kC;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 4, c16 = i & 15;
+      const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
+      umma::cp_async16(aQ + dst, q + (size_t)b * a.q_st.b + (size_t)(tb + row) * a.q_st.l + c16 * 8);
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = tid + kThreads * m;
+      umma::cp_async16(aSt + 16u * i, tiles + (bh * (nchunk + 1) + cc) * 16384u + 16u * i);
+    }
+    umma::cp_async_commit();
+  };
+  prefetch_kva(nchunk - 1);
+  prefetch_qst(nchunk - 1);
+
 #ifdef M3_TC_TIMING
   const int ltid = tid;
   long long tmark_ = clock64();
@@ -170,33 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int c = nchunk - 1; c >= 0 && ok; --c) {
     const int t0 = c * kC, tg = t0 + t;
     const float alast = ss->alast;
-    // ---- P0: raw tiles (cp.async), per-token scalars, g and e^A g -------------------------
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const int i = tid + kThreads * m;
-      const int row = i >> 4, c16 = i & 15;
-      const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
-      umma::cp_async16(aQ + dst, q + (size_t)b * a.q_st.b + (size_t)(t0 + row) * a.q_st.l + c16 * 8);
-      umma::cp_async16(aK + dst, k + (size_t)b * a.k_st.b + (size_t)(t0 + row) * a.k_st.l + c16 * 8);
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int i = tid + kThreads * m;
-      const int row = i >> 3, c8 = i & 7;
-      umma::cp_async16(aV + umma::sw128_off(row, c8),
-                       v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(t0 + row) * a.v_st.l + c8 * 8);
-      umma::cp_async16(aSt + 16u * i, tiles + (bh * (nchunk + 1) + c) * 16384u + 16u * i);
-    }
-    {
-      const int n4 = Nr >> 2;  // 16-byte chunks per angle row
-      const uint32_t aAng = umma::smem_u32(sm + kAng);
-      for (int i = tid; i < kC * n4; i += kThreads) {
-        const int row = i / n4, c4 = i - row * n4;
-        umma::cp_async16(aAng + row * 256 + 16 * (c4 ^ (row & 15)),
-                         a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + row) * a.ang_st.l + 4 * c4);
-      }
-    }
-    umma::cp_async_commit();
+    // ---- P0: per-token scalars, g and e^A g (this chunk's tiles were prefetched) ---------
     const size_t ro = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
     const float dt = softplusf(a.dt_raw[ro] + dtb);
     const float lam = sigmoidf_(a.trap_raw[ro]);
@@ -743,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncthreads();
+    if (c > 0) prefetch_kva(c - 1);  // the k, v and dw / angle tiles are free now
 
     M3_TC_MARK(16);
     // ---- per-token scalars: dadt (suffix of dA + the A_last term), preprocess adjoint -------
@@ -820,8 +842,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
+    if (c > 0) prefetch_qst(c - 1);
     M3_TC_MARK(18);
   }
+  umma::cp_async_wait_all();  // nothing of ours still lands in shared memory after an early exit
 
   if (ok) {
     // ---- seeds (kernel_bwd.py:636-646), angle carry, per-head reductions ------------------
