@@ -54,6 +54,13 @@ __device__ __forceinline__ uint32_t f2bf(float2 v) {
   return *reinterpret_cast<uint32_t*>(&t);
 }
 
+// Eight consecutive floats with one 256-bit load (sm_100; the address is 32-byte aligned).
+__device__ __forceinline__ void ldg8(const float* p, float (&v)[8]) {
+  asm volatile("ld.global.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "l"(p));
+}
+
 // sin / cos of an angle in [0, 2 pi) through the SFU (accurate on [-pi, pi]).
 __device__ __forceinline__ void sincos_wrapped(float x, float* s, float* c) {
   if (x >= kPi) x -= kTwoPi;

@@ -156,6 +156,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
     const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
     const int nchunk = L / kC;
     const int chunk_sub = a.dims.chunk / kC;
+    // 32-byte rotary-group pieces of the angle (or phi) rows can be read with one load
+    const bool ang32 = RAW ? ((uintptr_t)a.angles % 32 == 0 && a.ang_st.l % 8 == 0 && a.ang_st.b % 8 == 0)
+                           : ((uintptr_t)a.phi % 32 == 0 && Nr % 8 == 0);
     const uint32_t sQ = umma::smem_u32(sm + kQ), sK = umma::smem_u32(sm + kK), sV = umma::smem_u32(sm + kV);
     const uint32_t sVd = umma::smem_u32(sm + kVd), sSt = umma::smem_u32(sm + kSt);
     bool ok = true;
@@ -325,10 +328,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
               const int tgl = t0 + tb + j;
               const float* pp = RAW ? a.angles + (size_t)b * a.ang_st.b + (size_t)tgl * a.ang_st.l + 8 * g
                                     : a.phi + (bh * L + tgl) * Nr + 8 * g;
-              const float4 lo = *reinterpret_cast<const float4*>(pp);
-              const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
-              ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
-              ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
+              if (ang32) {
+                ldg8(pp, ph[j]);
+              } else {
+                const float4 lo = *reinterpret_cast<const float4*>(pp);
+                const float4 hi = *reinterpret_cast<const float4*>(pp + 4);
+                ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
+                ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
+              }
             }
             if (RAW) {
               const float2 w = mul2(*reinterpret_cast<const float2*>(dts + tb), f2s(kPi));
@@ -487,11 +494,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       }
       umma::fence_after_sync();
 
-      // the khat tile is free until the next chunk: stage this thread's z row pieces there
+      // the khat tile is free until the next chunk: stage the chunk's z rows there (rows of
+      // 128 bytes, four per warp instruction)
       if (!STATES && z) {
-        const __nv_bfloat16* zr = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half;
+        const __nv_bfloat16* zb = z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)t0 * a.z_st.l;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) umma::cp_async16(sK + umma::sw128_off(t, 4 * half + j), zr + 8 * j);
+        for (int m = 0; m < 4; ++m) {
+          const int i = ltid + kSlotThreads * m, row = i >> 3, c8 = i & 7;
+          umma::cp_async16(sK + umma::sw128_off(row, c8), zb + (size_t)row * a.z_st.l + 8 * c8);
+        }
       }
       umma::cp_async_commit();
       M3_TC_MARK(4);
@@ -574,8 +585,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       // ---- phase 6: output -----------------------------------------------------------------
       {
         const float2 eA = f2s(exp2f(A)), dg2 = f2s(dg);
-        __nv_bfloat16* yr = y + (size_t)b * a.y_st.b + (size_t)h * a.y_st.h + (size_t)tg * a.y_st.l + 32 * half;
-        if (z) asm volatile("cp.async.wait_group %0;" ::"n"(1) : "memory");  // the z group (committed before q~ / v)
+        if (z) {  // the z group (committed before q~ / v) of every thread of the slot
+          asm volatile("cp.async.wait_group %0;" ::"n"(1) : "memory");
+          slot_sync(slot);
+        }
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {  // 16 columns at a time
           float yi[16], ya[16];
@@ -604,14 +617,26 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
               packed[4 * j + e] = f2bf(r);
             }
           }
-          *reinterpret_cast<uint4*>(yr + 16 * hh) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          *reinterpret_cast<uint4*>(yr + 16 * hh + 8) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+          // y row pieces into the (free) vd tile; stored below as whole rows
+          *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + 2 * hh)) =
+              make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          *reinterpret_cast<uint4*>(sm + kVd + umma::sw128_off(t, 4 * half + 2 * hh + 1)) =
+              make_uint4(packed[4], packed[5], packed[6], packed[7]);
         }
       }
       umma::cp_async_wait_all();  // z reads done and nothing of ours still lands in the khat tile
       umma::fence_before_sync();
       slot_sync(slot);
       umma::fence_after_sync();
+      {
+        __nv_bfloat16* yb = y + (size_t)b * a.y_st.b + (size_t)h * a.y_st.h + (size_t)t0 * a.y_st.l;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int i = ltid + kSlotThreads * m, row = i >> 3, c8 = i & 7;
+          *reinterpret_cast<uint4*>(yb + (size_t)row * a.y_st.l + 8 * c8) =
+              *reinterpret_cast<const uint4*>(sm + kVd + umma::sw128_off(row, c8));
+        }
+      }
       if (c + 1 < nchunk) prefetch_k(c + 1);
       umma::fence_before_sync();
       slot_sync(slot);
