@@ -418,6 +418,43 @@ def run_reference(args, world, rank):
     return 0
 
 
+def run_profile_case(which):
+    """Three launches of one path on a case small enough for a full ncu capture.  Its inputs
+    (v, z, y 67 MB each at L = 2048) are still larger than L2."""
+    torch.cuda.set_device(0)
+    if which == "decode":
+        from mamba3_b200 import kernel_decode as KD
+        from mamba3_b200.state import SISOState
+        B, H, P, N, Nr = 256, 64, 64, 128, 32
+        g = torch.Generator(device="cuda").manual_seed(7)
+        r = lambda *sh, dt=torch.float32: torch.randn(*sh, device="cuda", generator=g).to(dt)
+        st = SISOState(ssm=r(B, H, P, N), k=r(B, H, N), v=r(B, H, P), phi=r(B, H, Nr))
+        raw = r(B, 3, H) * 0.1
+        for _ in range(3):
+            KD.siso_decode_raw(r(B, N, dt=torch.bfloat16), r(B, N, dt=torch.bfloat16), r(B, H, P, dt=torch.bfloat16),
+                               raw[:, 0], raw[:, 1], raw[:, 2], r(B, Nr), r(H), r(H, N), r(H, N), st,
+                               d_skip=r(H), z=r(B, H, P, dt=torch.bfloat16), dtype_policy="bf16")
+        torch.cuda.synchronize()
+        return 0
+    c = dict(CFG2, L=2048)
+    d = make_cfg2_inputs(c, 0)
+    if which == "fwd":
+        for _ in range(3):
+            fwd_call(d, c)
+    else:
+        from mamba3_b200 import kernel_bwd as KB
+        ws = torch.empty(KB.workspace_bytes(c["B"], c["L"], c["H"], c["N"], c["P"], c["Nr"], c["chunk"]),
+                         dtype=torch.uint8, device="cuda")
+        v, z, dy = (d[n].permute(0, 2, 1, 3) for n in ("x", "z", "dy"))
+        for _ in range(3):
+            fwd_call(d, c)
+            KB.siso_backward_raw(dy, d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                                 d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z, chunk=c["chunk"],
+                                 dtype_policy="bf16", workspace=ws)
+    torch.cuda.synchronize()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,8 +462,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,cpu or all")
+    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode"],
+                    help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
+                         "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile:
+        return run_profile_case(args.profile)
 
     world, rank, local = dist_setup() if args.impl == "ours" else (
         int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
