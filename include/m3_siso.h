@@ -199,8 +199,8 @@ typedef struct M3DecodeArgs {
 int m3_siso_decode(const M3DecodeArgs *args, void *stream);
 
 /* Device-side error word: non-zero if a kernel gave up on a bounded wait for the tensor
- * core (the kernel then winds down instead of spinning).  Synchronises the device.
- * `reset` != 0 clears it. */
+ * core or for a bulk copy (the kernel then winds down instead of spinning).  Synchronises
+ * the device.  `reset` != 0 clears it. */
 int m3_device_error(int reset);
 
 /* Last error message of this thread ("" if none). */

@@ -95,7 +95,10 @@ const char* m3_last_error(void) { return g_err.c_str(); }
 
 int m3_version(void) { return 1; }
 
-int m3_device_error(int reset) { return read_device_error(reset); }
+int m3_device_error(int reset) {
+  const int f = read_device_error(reset), d = read_decode_error(reset);
+  return f != 0 ? f : d;
+}
 
 int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   g_err.clear();

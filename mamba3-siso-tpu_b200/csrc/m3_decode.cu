@@ -6,8 +6,32 @@ namespace m3 {
 
 template <int N, int P, typename T, bool MMB>
 static int run_decode(const M3DecodeArgs& a, cudaStream_t s) {
-  decode_kernel<N, P, T, MMB><<<a.batch * a.nheads, kDecThreads, 0, s>>>(a);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int sms[64] = {};
+  static bool attr[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(M3_ERR_LAUNCH, "device index out of range");
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  if (!attr[dev]) {
+    if (cudaFuncSetAttribute(decode_kernel<N, P, T, MMB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)DecSmem<N, P>::kBytes) != cudaSuccess)
+      return check_launch("m3_siso_decode: cudaFuncSetAttribute");
+    attr[dev] = true;
+  }
+  const int items = a.batch * a.nheads;
+  const int grid = items < sms[dev] * kDecCtasPerSm ? items : sms[dev] * kDecCtasPerSm;
+  decode_kernel<N, P, T, MMB><<<grid, kDecThreads, DecSmem<N, P>::kBytes, s>>>(a);
   return check_launch("m3_siso_decode");
+}
+
+int read_decode_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_m3_dec_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_m3_dec_error, &zero, sizeof(int));
+  }
+  return v;
 }
 
 int launch_decode(const M3DecodeArgs& a, cudaStream_t s) {

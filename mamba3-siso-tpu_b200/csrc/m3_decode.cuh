@@ -7,133 +7,205 @@
 //   y    = (S' q~ + D v) * silu(z)
 //
 // A bandwidth-bound read-modify-write of the (P, N) fp32 state, which is touched once.
-// One CTA per (b, h).  A preamble computes, once per CTA, the rotated q~ / k~ columns and
-// the per-row coefficients beta v_prev, gamma v and the gate into shared memory; then the
-// state streams through in whole rows (a warp instruction covers 32 consecutive float4
-// of the state, one 512-byte row at N = 128) with packed fp32x2 arithmetic, and the
-// readout S' q~ is a shuffle reduction over the lanes of a row.  The state, k, v and phi
-// buffers are updated in place.
+// A persistent grid (a few CTAs per SM) walks the (b, h) items; each CTA streams the
+// states through two shared-memory buffers with bulk copies (cp.async.bulk, completion on
+// an mbarrier, no register staging): while item i is updated in one buffer, item i + grid
+// is already on its way into the other, and item i goes back to HBM with a bulk store.
+// Per item a preamble computes the rotated q~ / k~ columns and the per-row coefficients
+// beta v_prev, gamma v, D v and silu(z) into shared memory (its global loads overlap the
+// state copy).  The update runs over consecutive float4 of the state (whole rows per
+// warp instruction at N = 128) with packed fp32x2 arithmetic; the readout S' q~ is a
+// shuffle reduction over the lanes of a row.  The state, k, v and phi buffers are updated
+// in place.  Every wait is bounded: on time-out the kernel records an error and returns.
 #pragma once
 
 #include "m3_common.cuh"
+#include "m3_umma.cuh"
 
 namespace m3 {
 
 constexpr int kDecThreads = 256;
+constexpr int kDecCtasPerSm = 3;
+
+__device__ int g_m3_dec_error;  // non-zero after a bounded wait of the decode kernel gave up
+
+namespace bulk {
+__device__ __forceinline__ void expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(mbar)), "r"(bytes)
+               : "memory");
+}
+// global -> shared, completion counted on `mbar` (no multicast)
+__device__ __forceinline__ void load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   umma::smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(umma::smem_u32(mbar))
+               : "memory");
+}
+// shared -> global, tracked by this thread's bulk groups
+__device__ __forceinline__ void store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(umma::smem_u32(smem_src)),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void wait_reads() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+}  // namespace bulk
+
+template <int N, int P>
+struct DecSmem {
+  static constexpr uint32_t kStateBytes = P * N * 4;
+  static constexpr size_t kBytes = 2 * (size_t)kStateBytes;  // the two state buffers (dynamic)
+};
 
 template <int N, int P, typename T, bool MMB>
-__global__ void __launch_bounds__(kDecThreads, 4) decode_kernel(const M3DecodeArgs a) {
-  static_assert(N <= 128 && P <= 128 && N % 4 == 0, "decode tiling");
+__global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(const M3DecodeArgs a) {
+  static_assert(N <= 128 && P <= 128 && N % 4 == 0 && (P * N / 4) % 32 == 0, "decode tiling");
   constexpr int LPR = N / 4;              // lanes (float4 columns) per state row
   constexpr int NF4 = P * N / 4;          // float4 of one (b, h) state
   constexpr int EPT = (NF4 + kDecThreads - 1) / kDecThreads;
   constexpr int H2 = N / 2;
+  constexpr uint32_t kBytes = DecSmem<N, P>::kStateBytes;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ uint64_t mbar[2];
   __shared__ __align__(16) float s_q[N], s_k[N], s_kp[N];  // q~ (readout-rounded), k~, previous k~
   __shared__ float s_bv[P], s_gv[P], s_dv[P], s_gate[P];  // beta v_prev, gamma v, D v, silu(z)
   __shared__ float s_ph[64];
   const int tid = threadIdx.x;
   const int H = a.nheads, Nr = a.n_angles;
-  const int b = blockIdx.x / H, h = blockIdx.x % H;
-  const size_t bh = (size_t)b * H + h;
+  const int total = a.batch * H;
+  auto buf = [&](int sel) { return reinterpret_cast<float4*>(dsm + (size_t)sel * kBytes); };
 
-  // ---- the state: every load in flight first ---------------------------------------------
-  float4* st4 = reinterpret_cast<float4*>(a.ssm + bh * P * N);
-  float4 S[EPT];
-#pragma unroll
-  for (int m = 0; m < EPT; ++m) {
-    const int i = tid + kDecThreads * m;
-    if (i < NF4) S[m] = __ldcs(st4 + i);
-  }
-
-  // ---- scalars (raw == 1 fuses model.py:274-277) -----------------------------------
-  float adt, dt, lam;
-  if (a.raw) {
-    const size_t o = (size_t)b * a.raw_stride_b + h;
-    dt = softplusf(a.dt_raw[o] + a.dt_bias[h]);
-    adt = fminf(-heavy_tail(a.a_raw[o]), -a.a_floor) * dt;
-    lam = sigmoidf_(a.trap_raw[o]);
-  } else {
-    adt = a.adt[bh];
-    dt = a.dt[bh];
-    lam = a.lam[bh];
-  }
-  const float alpha = expf(adt);
-  const float beta = alpha * dt * (1.f - lam);
-  const float gamma = dt * lam;
-
-  // ---- preamble: advanced angles; per-row coefficients -------------------------------------
-  if (tid < Nr)
-    s_ph[tid] = wrap_fast(a.phi[bh * Nr + tid] + tanh_acc(a.angles[(size_t)b * a.ang_stride_b + tid]) * kPi * dt);
-  if (tid >= 128 && tid < 128 + P) {
-    const int p = tid - 128;
-    const T* vrow = (const T*)a.v + (size_t)b * a.vz_stride_b + (size_t)h * P;
-    const float vc = ld(vrow + p);
-    const float vp = a.state_v[bh * P + p];
-    s_bv[p] = beta * vp;
-    s_gv[p] = gamma * vc;
-    s_dv[p] = a.d_skip ? a.d_skip[h] * vc : 0.f;
-    float gate = 1.f;
-    if (a.z) {
-      const float zz = ld((const T*)a.z + (size_t)b * a.vz_stride_b + (size_t)h * P + p);
-      gate = zz * sigmoidf_(zz);
-    }
-    s_gate[p] = gate;
-    a.state_v[bh * P + p] = vc;
+  if (tid == 0) {
+    umma::mbar_init(&mbar[0], 1);
+    umma::mbar_init(&mbar[1], 1);
+    umma::fence_mbar_init();
   }
   __syncthreads();
-  // rotary columns: x cos + rot_half(x) sin, rot_half = [-hi, lo]  (layout.py:375-398)
-  if (tid < N) {
+  int it = blockIdx.x;
+  if (tid == 0 && it < total) {
+    bulk::expect_tx(&mbar[0], kBytes);
+    bulk::load(buf(0), a.ssm + (size_t)it * P * N, kBytes, &mbar[0]);
+  }
+
+  for (int kk = 0; it < total; it += gridDim.x, ++kk) {
+    const int sel = kk & 1;
+    const int nxt = it + gridDim.x;
+    if (tid == 0 && nxt < total) {
+      bulk::wait_reads();  // the store that last read the other buffer has read it
+      bulk::expect_tx(&mbar[sel ^ 1], kBytes);
+      bulk::load(buf(sel ^ 1), a.ssm + (size_t)nxt * P * N, kBytes, &mbar[sel ^ 1]);
+    }
+    const int b = it / H, h = it % H;
+    const size_t bh = (size_t)it;
+
+    // ---- scalars (raw == 1 fuses model.py:274-277) -----------------------------------
+    float adt, dt, lam;
+    if (a.raw) {
+      const size_t o = (size_t)b * a.raw_stride_b + h;
+      dt = softplusf(a.dt_raw[o] + a.dt_bias[h]);
+      adt = fminf(-heavy_tail(a.a_raw[o]), -a.a_floor) * dt;
+      lam = sigmoidf_(a.trap_raw[o]);
+    } else {
+      adt = a.adt[bh];
+      dt = a.dt[bh];
+      lam = a.lam[bh];
+    }
+    const float alpha = expf(adt);
+    const float beta = alpha * dt * (1.f - lam);
+    const float gamma = dt * lam;
+
+    // ---- preamble: column operands (loads first), advanced angles, per-row coefficients ----
+    float u = 0.f, w = 0.f, um = 0.f, wm = 0.f, kpv = 0.f;
     const int n = tid, j = n < H2 ? n : n - H2;
-    const T* q = (const T*)a.q + (size_t)b * a.qk_stride_b;
-    const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
-    const float u = ld(q + n) + a.q_bias[h * N + n];
-    const float w = ld(k + n) + a.k_bias[h * N + n];
-    float qv = u, kv = w;
-    if (j < Nr) {
+    if (tid < N) {
+      const T* q = (const T*)a.q + (size_t)b * a.qk_stride_b;
+      const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
       const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
-      const float um = ld(q + mm) + a.q_bias[h * N + mm];
-      const float wm = ld(k + mm) + a.k_bias[h * N + mm];
-      float sn, cs;
-      sincos_wrapped(s_ph[j], &sn, &cs);
-      const float sgn = n < H2 ? -1.f : 1.f;
-      qv = u * cs + sgn * um * sn;
-      kv = w * cs + sgn * wm * sn;
+      u = ld(q + n) + a.q_bias[h * N + n];
+      w = ld(k + n) + a.k_bias[h * N + n];
+      if (j < Nr) {
+        um = ld(q + mm) + a.q_bias[h * N + mm];
+        wm = ld(k + mm) + a.k_bias[h * N + mm];
+      }
+      kpv = a.state_k[bh * N + n];
     }
-    s_q[n] = mmr<MMB>(qv);
-    s_k[n] = kv;
-    s_kp[n] = a.state_k[bh * N + n];
-    a.state_k[bh * N + n] = kv;
-  }
-  if (tid < Nr) a.phi[bh * Nr + tid] = s_ph[tid];  // nobody reads the old phi any more
-  __syncthreads();
+    if (tid < Nr)
+      s_ph[tid] = wrap_fast(a.phi[bh * Nr + tid] + tanh_acc(a.angles[(size_t)b * a.ang_stride_b + tid]) * kPi * dt);
+    if (tid >= 128 && tid < 128 + P) {
+      const int p = tid - 128;
+      const T* vrow = (const T*)a.v + (size_t)b * a.vz_stride_b + (size_t)h * P;
+      const float vc = ld(vrow + p);
+      const float vp = a.state_v[bh * P + p];
+      s_bv[p] = beta * vp;
+      s_gv[p] = gamma * vc;
+      s_dv[p] = a.d_skip ? a.d_skip[h] * vc : 0.f;
+      float gate = 1.f;
+      if (a.z) {
+        const float zz = ld((const T*)a.z + (size_t)b * a.vz_stride_b + (size_t)h * P + p);
+        gate = zz * sigmoidf_(zz);
+      }
+      s_gate[p] = gate;
+      a.state_v[bh * P + p] = vc;
+    }
+    __syncthreads();
+    // rotary columns: x cos + rot_half(x) sin, rot_half = [-hi, lo]  (layout.py:375-398)
+    if (tid < N) {
+      float qv = u, kv = w;
+      if (j < Nr) {
+        float sn, cs;
+        sincos_wrapped(s_ph[j], &sn, &cs);
+        const float sgn = n < H2 ? -1.f : 1.f;
+        qv = u * cs + sgn * um * sn;
+        kv = w * cs + sgn * wm * sn;
+      }
+      s_q[n] = mmr<MMB>(qv);
+      s_k[n] = kv;
+      s_kp[n] = kpv;
+      a.state_k[bh * N + n] = kv;
+    }
+    if (tid < Nr) a.phi[bh * Nr + tid] = s_ph[tid];  // nobody reads the old phi any more
 
-  // ---- S' = alpha S + (beta v_prev) k_prev^T + (gamma v) k~^T; y = (S' q~ + D v) silu(z) -----
-  const int c4 = tid % LPR;
-  const float4 q4 = *reinterpret_cast<const float4*>(s_q + 4 * c4);
-  const float4 k4 = *reinterpret_cast<const float4*>(s_k + 4 * c4);
-  const float4 kp4 = *reinterpret_cast<const float4*>(s_kp + 4 * c4);
-  const float2 al2 = f2s(alpha);
-  T* yrow = (T*)a.y + bh * P;
-#pragma unroll
-  for (int m = 0; m < EPT; ++m) {
-    const int i = tid + kDecThreads * m;
-    if (NF4 % kDecThreads != 0 && i >= NF4) break;  // NF4 % 32 == 0: whole warps stop together
-    const int p = i / LPR;
-    const float2 bv = f2s(s_bv[p]), gv = f2s(s_gv[p]);
-    const float2 s01 = fma2(al2, f2(S[m].x, S[m].y), fma2(bv, f2(kp4.x, kp4.y), mul2(gv, f2(k4.x, k4.y))));
-    const float2 s23 = fma2(al2, f2(S[m].z, S[m].w), fma2(bv, f2(kp4.z, kp4.w), mul2(gv, f2(k4.z, k4.w))));
-    __stcs(st4 + i, make_float4(s01.x, s01.y, s23.x, s23.y));
-    float2 r01 = s01, r23 = s23;
-    if (MMB) {  // bf16 readout operands (kernel_decode.py, BF16 policy)
-      r01 = bf2f(f2bf(s01));
-      r23 = bf2f(f2bf(s23));
+    // ---- this item's state has landed ------------------------------------------------------
+    if (__syncthreads_or(!umma::mbar_wait(&mbar[sel], (kk >> 1) & 1))) {
+      if (tid == 0) atomicExch(&g_m3_dec_error, 21);
+      break;
     }
-    const float2 pr = fma2(r23, f2(q4.z, q4.w), mul2(r01, f2(q4.x, q4.y)));
-    float part = pr.x + pr.y;
+
+    // ---- S' = alpha S + (beta v_prev) k_prev^T + (gamma v) k~^T; y = (S' q~ + D v) silu(z) -----
+    float4* st = buf(sel);
+    const int c4 = tid % LPR;
+    const float4 q4 = *reinterpret_cast<const float4*>(s_q + 4 * c4);
+    const float4 k4 = *reinterpret_cast<const float4*>(s_k + 4 * c4);
+    const float4 kp4 = *reinterpret_cast<const float4*>(s_kp + 4 * c4);
+    const float2 al2 = f2s(alpha);
+    T* yrow = (T*)a.y + bh * P;
 #pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (c4 == 0) stg<T>(yrow + p, (part + s_dv[p]) * s_gate[p]);
+    for (int m = 0; m < EPT; ++m) {
+      const int i = tid + kDecThreads * m;
+      if (NF4 % kDecThreads != 0 && i >= NF4) break;  // NF4 % 32 == 0: whole warps stop together
+      const int p = i / LPR;
+      const float4 S = st[i];
+      const float2 bv = f2s(s_bv[p]), gv = f2s(s_gv[p]);
+      const float2 s01 = fma2(al2, f2(S.x, S.y), fma2(bv, f2(kp4.x, kp4.y), mul2(gv, f2(k4.x, k4.y))));
+      const float2 s23 = fma2(al2, f2(S.z, S.w), fma2(bv, f2(kp4.z, kp4.w), mul2(gv, f2(k4.z, k4.w))));
+      st[i] = make_float4(s01.x, s01.y, s23.x, s23.y);
+      float2 r01 = s01, r23 = s23;
+      if (MMB) {  // bf16 readout operands (kernel_decode.py, BF16 policy)
+        r01 = bf2f(f2bf(s01));
+        r23 = bf2f(f2bf(s23));
+      }
+      const float2 pr = fma2(r23, f2(q4.z, q4.w), mul2(r01, f2(q4.x, q4.y)));
+      float part = pr.x + pr.y;
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (c4 == 0) stg<T>(yrow + p, (part + s_dv[p]) * s_gate[p]);
+    }
+    umma::fence_async_smem();  // this thread's state writes, for the bulk store
+    __syncthreads();
+    if (tid == 0) bulk::store(a.ssm + (size_t)it * P * N, st, kBytes);
   }
+  if (tid == 0) bulk::wait_all();  // the stores have finished before the CTA's shared memory goes away
 }
 
 }  // namespace m3
