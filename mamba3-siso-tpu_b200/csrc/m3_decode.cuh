@@ -88,6 +88,54 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
     bulk::load(buf(0), a.ssm + (size_t)it * P * N, kBytes, &mbar[0]);
   }
 
+  // Global inputs of one item's preamble, loaded one item ahead (in registers) so that their
+  // latency overlaps the previous item's update.
+  struct In {
+    float dtr, ar, trr;       // raw dt / A / trap (or adt / dt / lam)
+    float u, w, um, wm, kpv;  // column threads: q + q_bias, k + k_bias, their pair partners, k_prev
+    float ph, an;             // angle threads: phi, raw angle
+    float vc, vp, zz;         // row threads: v, v_prev, z
+  };
+  const int n = tid, j = n < H2 ? n : n - H2;
+  auto load_in = [&](int item, In& x) {
+    const int b = item / H, h = item % H;
+    const size_t bh = (size_t)item;
+    if (a.raw) {
+      const size_t o = (size_t)b * a.raw_stride_b + h;
+      x.dtr = a.dt_raw[o] + a.dt_bias[h];
+      x.ar = a.a_raw[o];
+      x.trr = a.trap_raw[o];
+    } else {
+      x.dtr = a.adt[bh];
+      x.ar = a.dt[bh];
+      x.trr = a.lam[bh];
+    }
+    if (tid < N) {
+      const T* q = (const T*)a.q + (size_t)b * a.qk_stride_b;
+      const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
+      const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
+      x.u = ld(q + n) + a.q_bias[h * N + n];
+      x.w = ld(k + n) + a.k_bias[h * N + n];
+      if (j < Nr) {
+        x.um = ld(q + mm) + a.q_bias[h * N + mm];
+        x.wm = ld(k + mm) + a.k_bias[h * N + mm];
+      }
+      x.kpv = a.state_k[bh * N + n];
+    }
+    if (tid < Nr) {
+      x.ph = a.phi[bh * Nr + tid];
+      x.an = a.angles[(size_t)b * a.ang_stride_b + tid];
+    }
+    if (tid >= 128 && tid < 128 + P) {
+      const int p = tid - 128;
+      x.vc = ld((const T*)a.v + (size_t)b * a.vz_stride_b + (size_t)h * P + p);
+      x.vp = a.state_v[bh * P + p];
+      x.zz = a.z ? ld((const T*)a.z + (size_t)b * a.vz_stride_b + (size_t)h * P + p) : 0.f;
+    }
+  };
+  In cur{};
+  if (it < total) load_in(it, cur);
+
   for (int kk = 0; it < total; it += gridDim.x, ++kk) {
     const int sel = kk & 1;
     const int nxt = it + gridDim.x;
@@ -96,72 +144,50 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
       bulk::expect_tx(&mbar[sel ^ 1], kBytes);
       bulk::load(buf(sel ^ 1), a.ssm + (size_t)nxt * P * N, kBytes, &mbar[sel ^ 1]);
     }
-    const int b = it / H, h = it % H;
+    In nx{};
+    if (nxt < total) load_in(nxt, nx);
+    const int h = it % H;
     const size_t bh = (size_t)it;
 
     // ---- scalars (raw == 1 fuses model.py:274-277) -----------------------------------
     float adt, dt, lam;
     if (a.raw) {
-      const size_t o = (size_t)b * a.raw_stride_b + h;
-      dt = softplusf(a.dt_raw[o] + a.dt_bias[h]);
-      adt = fminf(-heavy_tail(a.a_raw[o]), -a.a_floor) * dt;
-      lam = sigmoidf_(a.trap_raw[o]);
+      dt = softplusf(cur.dtr);
+      adt = fminf(-heavy_tail(cur.ar), -a.a_floor) * dt;
+      lam = sigmoidf_(cur.trr);
     } else {
-      adt = a.adt[bh];
-      dt = a.dt[bh];
-      lam = a.lam[bh];
+      adt = cur.dtr;
+      dt = cur.ar;
+      lam = cur.trr;
     }
     const float alpha = expf(adt);
     const float beta = alpha * dt * (1.f - lam);
     const float gamma = dt * lam;
 
-    // ---- preamble: column operands (loads first), advanced angles, per-row coefficients ----
-    float u = 0.f, w = 0.f, um = 0.f, wm = 0.f, kpv = 0.f;
-    const int n = tid, j = n < H2 ? n : n - H2;
-    if (tid < N) {
-      const T* q = (const T*)a.q + (size_t)b * a.qk_stride_b;
-      const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
-      const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
-      u = ld(q + n) + a.q_bias[h * N + n];
-      w = ld(k + n) + a.k_bias[h * N + n];
-      if (j < Nr) {
-        um = ld(q + mm) + a.q_bias[h * N + mm];
-        wm = ld(k + mm) + a.k_bias[h * N + mm];
-      }
-      kpv = a.state_k[bh * N + n];
-    }
-    if (tid < Nr)
-      s_ph[tid] = wrap_fast(a.phi[bh * Nr + tid] + tanh_acc(a.angles[(size_t)b * a.ang_stride_b + tid]) * kPi * dt);
+    // ---- preamble: advanced angles, per-row coefficients --------------------------------------
+    if (tid < Nr) s_ph[tid] = wrap_fast(cur.ph + tanh_acc(cur.an) * kPi * dt);
     if (tid >= 128 && tid < 128 + P) {
       const int p = tid - 128;
-      const T* vrow = (const T*)a.v + (size_t)b * a.vz_stride_b + (size_t)h * P;
-      const float vc = ld(vrow + p);
-      const float vp = a.state_v[bh * P + p];
-      s_bv[p] = beta * vp;
-      s_gv[p] = gamma * vc;
-      s_dv[p] = a.d_skip ? a.d_skip[h] * vc : 0.f;
-      float gate = 1.f;
-      if (a.z) {
-        const float zz = ld((const T*)a.z + (size_t)b * a.vz_stride_b + (size_t)h * P + p);
-        gate = zz * sigmoidf_(zz);
-      }
-      s_gate[p] = gate;
-      a.state_v[bh * P + p] = vc;
+      s_bv[p] = beta * cur.vp;
+      s_gv[p] = gamma * cur.vc;
+      s_dv[p] = a.d_skip ? a.d_skip[h] * cur.vc : 0.f;
+      s_gate[p] = a.z ? cur.zz * sigmoidf_(cur.zz) : 1.f;
+      a.state_v[bh * P + p] = cur.vc;
     }
     __syncthreads();
     // rotary columns: x cos + rot_half(x) sin, rot_half = [-hi, lo]  (layout.py:375-398)
     if (tid < N) {
-      float qv = u, kv = w;
+      float qv = cur.u, kv = cur.w;
       if (j < Nr) {
         float sn, cs;
         sincos_wrapped(s_ph[j], &sn, &cs);
         const float sgn = n < H2 ? -1.f : 1.f;
-        qv = u * cs + sgn * um * sn;
-        kv = w * cs + sgn * wm * sn;
+        qv = cur.u * cs + sgn * cur.um * sn;
+        kv = cur.w * cs + sgn * cur.wm * sn;
       }
       s_q[n] = mmr<MMB>(qv);
       s_k[n] = kv;
-      s_kp[n] = kpv;
+      s_kp[n] = cur.kpv;
       a.state_k[bh * N + n] = kv;
     }
     if (tid < Nr) a.phi[bh * Nr + tid] = s_ph[tid];  // nobody reads the old phi any more
@@ -204,6 +230,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
     umma::fence_async_smem();  // this thread's state writes, for the bulk store
     __syncthreads();
     if (tid == 0) bulk::store(a.ssm + (size_t)it * P * N, st, kBytes);
+    cur = nx;
   }
   if (tid == 0) bulk::wait_all();  // the stores have finished before the CTA's shared memory goes away
 }
