@@ -53,8 +53,10 @@ struct Small {
   float wtot[4];
   float red[8];
   float A[128];
+  float bias[2 * kN];  // the head's q_bias, k_bias
 };
-constexpr size_t kSmemBytes = kTiles + 1024 + 1024;  // tiles + Small (<= 1 KB) + alignment slack
+constexpr size_t kSmemBytes = kTiles + 2048 + 1024;  // tiles + Small (<= 2 KB) + alignment slack
+static_assert(sizeof(Small) <= 2048, "Small must fit its 2 KB slot");
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint4* rks = rqs + 16 * kC;                                                      // [16][128]: raw k
 
   if (warp == 0) umma::tmem_alloc(&ss->tmem, 512);
+  ss->bias[tid] = tid < kN ? a.q_bias[h * kN + tid] : a.k_bias[h * kN + tid - kN];
   if (tid == 0) {
     for (int i = 0; i < 3; ++i) umma::mbar_init(&ss->mbar[i], 1);
     umma::fence_mbar_init();
@@ -288,8 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* uws = reinterpret_cast<float*>(sm + kScrUw);
       const int g = warp;
       const bool grot = 8 * g < Nr;
-      const float* qbp = a.q_bias + h * kN + 8 * g;
-      const float* kbp = a.k_bias + h * kN + 8 * g;
+      const float* qbp = ss->bias + 8 * g;
+      const float* kbp = ss->bias + kN + 8 * g;
       float off[8];
 #pragma unroll
       for (int r = 0; r < 8; ++r) off[r] = grot ? phis[(bh * nchunk + c) * Nr + 8 * g + r] : 0.f;
@@ -355,10 +358,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 4; ++e) {
             const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
             const float2 ns2 = f2(-sn[2 * e], -sn[2 * e + 1]);
-            const float2 ulo = add2(bf2f(ql[e]), __ldg(reinterpret_cast<const float2*>(qbp + 2 * e)));
-            const float2 uhi = add2(bf2f(qh[e]), __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e)));
-            const float2 wlo = add2(bf2f(kl[e]), __ldg(reinterpret_cast<const float2*>(kbp + 2 * e)));
-            const float2 whi = add2(bf2f(kh[e]), __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e)));
+            const float2 ulo = add2(bf2f(ql[e]), *reinterpret_cast<const float2*>(qbp + 2 * e));
+            const float2 uhi = add2(bf2f(qh[e]), *reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
+            const float2 wlo = add2(bf2f(kl[e]), *reinterpret_cast<const float2*>(kbp + 2 * e));
+            const float2 whi = add2(bf2f(kh[e]), *reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
             uw2 = fma2(ulo, wlo, uw2);
             uw2 = fma2(uhi, whi, uw2);
             pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
@@ -624,10 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t kl[4] = {uk0.x, uk0.y, uk0.z, uk0.w}, kh[4] = {uk1.x, uk1.y, uk1.z, uk1.w};
         float bq[16], bk[16];  // biases of pairs j0 .. j0+7: [0, 8) low halves, [8, 16) high halves
         {
-          const float4* qb4 = reinterpret_cast<const float4*>(a.q_bias + h * kN + j0);
-          const float4* kb4 = reinterpret_cast<const float4*>(a.k_bias + h * kN + j0);
-          const float4 v[8] = {__ldg(qb4), __ldg(qb4 + 1), __ldg(qb4 + 16), __ldg(qb4 + 17),
-                               __ldg(kb4), __ldg(kb4 + 1), __ldg(kb4 + 16), __ldg(kb4 + 17)};
+          const float4* qb4 = reinterpret_cast<const float4*>(ss->bias + j0);
+          const float4* kb4 = reinterpret_cast<const float4*>(ss->bias + kN + j0);
+          const float4 v[8] = {qb4[0], qb4[1], qb4[16], qb4[17], kb4[0], kb4[1], kb4[16], kb4[17]};
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
             bq[4 * m] = v[m].x; bq[4 * m + 1] = v[m].y; bq[4 * m + 2] = v[m].z; bq[4 * m + 3] = v[m].w;

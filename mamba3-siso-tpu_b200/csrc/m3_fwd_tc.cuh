@@ -55,6 +55,7 @@ constexpr int kThreads = 2 * kSlotThreads;
 constexpr uint32_t kQ = 0, kK = 32768, kV = 65536, kVd = 81920, kSt = 98304, kSlotBytes = 114688;
 // scratch laid over the vd tile while it is not live
 constexpr uint32_t kScrDt = 0, kScrScl = 512, kScrUw = 1024, kScrA = 0;  // uw: [8][128] floats
+constexpr uint32_t kScrBias = 5120;  // the head's q_bias, k_bias [2][128] (loaded with the khat prefetch)
 
 struct SlotSmall {
   uint64_t mbar[2];
@@ -226,6 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
         const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
         umma::cp_async16(sK + dst, k + (size_t)b * a.k_st.b + (size_t)(tb + row) * a.k_st.l + c16 * 8);
       }
+      if (ltid < 64)  // biases into the vd tile's scratch (its y staging has been stored by now)
+        umma::cp_async16(sVd + kScrBias + 16 * ltid, (ltid < 32 ? a.q_bias + h * kN : a.k_bias + h * kN - 128) + 4 * ltid);
       umma::cp_async_commit();
     };
     prefetch_qv(0);
@@ -313,8 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
         float* uws = reinterpret_cast<float*>(sm + kVd + kScrUw);  // [8 groups][128 tokens]
         const int g = lwarp;
         const bool grot = 8 * g < Nr;  // Nr % 8 == 0: a group rotates entirely or not at all
-        const float* qbp = a.q_bias + h * kN + 8 * g;
-        const float* kbp = a.k_bias + h * kN + 8 * g;
+        const float* qbp = reinterpret_cast<const float*>(sm + kVd + kScrBias) + 8 * g;
+        const float* kbp = qbp + kN;
         float off[8];
 #pragma unroll
         for (int r = 0; r < 8; ++r) off[r] = carry8[r];
@@ -373,10 +376,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
             for (int e = 0; e < 4; ++e) {
               const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
               const float2 ns2 = f2(-sn[2 * e], -sn[2 * e + 1]);
-              const float2 ulo = add2(bf2f(ql[e]), __ldg(reinterpret_cast<const float2*>(qbp + 2 * e)));
-              const float2 uhi = add2(bf2f(qh[e]), __ldg(reinterpret_cast<const float2*>(qbp + 64 + 2 * e)));
-              const float2 wlo = add2(bf2f(kl[e]), __ldg(reinterpret_cast<const float2*>(kbp + 2 * e)));
-              const float2 whi = add2(bf2f(kh[e]), __ldg(reinterpret_cast<const float2*>(kbp + 64 + 2 * e)));
+              const float2 ulo = add2(bf2f(ql[e]), *reinterpret_cast<const float2*>(qbp + 2 * e));
+              const float2 uhi = add2(bf2f(qh[e]), *reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
+              const float2 wlo = add2(bf2f(kl[e]), *reinterpret_cast<const float2*>(kbp + 2 * e));
+              const float2 whi = add2(bf2f(kh[e]), *reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
               uw2 = fma2(ulo, wlo, uw2);
               uw2 = fma2(uhi, whi, uw2);
               pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
