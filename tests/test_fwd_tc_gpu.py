@@ -57,6 +57,28 @@ def test_tc_raw_boundary(shape, seeded):
     assert rel_error(fs, fsg) < TOL
 
 
+def test_tc_raw_boundary_strong_decay():
+    """Large dt in the first half of the sequence: there the decay over a 32-token block
+    exceeds 2^64, so the mask takes its direct exp2(min(A_i - A_j, 0)) form; the second half
+    takes the factored form.  Both against the oracle."""
+    from mamba3_b200 import kernel_fwd as KF
+
+    b, h, l, n, p, nr, chunk = 2, 2, 512, 128, 64, 32, 128
+    x, _ = pre_inputs(b, h, l, n, p, nr, seed=11)
+    x["dt_raw"][:, : l // 2] += 3.0
+    x["dt_bias"] = torch.zeros(h, dtype=torch.float64)
+    y_ref, fin = O.siso_segment(_r(x["q"]), _r(x["k"]), _r(x["v"]), x["dt_raw"], x["a_raw"], x["trap_raw"],
+                                x["angles"], x["dt_bias"], x["q_bias"], x["k_bias"], x["d_skip"], _r(x["z"]),
+                                chunk=chunk, policy="bf16")
+    args = (dev(x["q"], B16), dev(x["k"], B16), dev(x["v"], B16), dev(x["dt_raw"]), dev(x["a_raw"]),
+            dev(x["trap_raw"]), dev(x["angles"]), dev(x["dt_bias"]), dev(x["q_bias"]), dev(x["k_bias"]),
+            dev(x["d_skip"]), dev(x["z"], B16))
+    y, fs, *_ = KF.siso_forward_raw(*args, kernel="tensorcore", chunk=chunk, dtype_policy="bf16")
+    assert torch.isfinite(y.float()).all()
+    assert rel_error(y, y_ref) < TOL
+    assert rel_error(fs, fin.ssm) < TOL
+
+
 @pytest.mark.parametrize("gate_skip", [True, False])
 def test_tc_preprocessed_boundary_with_residuals(gate_skip):
     from mamba3_b200 import kernel_fwd as KF
