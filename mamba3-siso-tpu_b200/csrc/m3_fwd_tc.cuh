@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
     auto prefetch_qv = [&](int cc) {
       const int tb = cc * kC;
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
+      for (int m = 0; m < (STATES ? 0 : 8); ++m) {
         const int i = ltid + kSlotThreads * m;  // 0 .. 2047
         const int row = i >> 4, c16 = i & 15;
         const uint32_t dst = (c16 >> 3) * 16384u + umma::sw128_off(row, c16 & 7);
@@ -363,8 +363,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
               if (grot) sincos_wrapped(wrap_fast(ph[j][r]), &sn[r], &cs[r]);
             }
             const uint32_t soff = umma::sw128_off(tt, g);
-            const uint4 uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
-            const uint4 uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+            uint4 uql = make_uint4(0u, 0u, 0u, 0u), uqh = uql;
+            if constexpr (!STATES) {  // the states-only sweep needs khat alone
+              uql = *reinterpret_cast<const uint4*>(sm + kQ + soff);
+              uqh = *reinterpret_cast<const uint4*>(sm + kQ + 16384 + soff);
+            }
             const uint4 ukl = *reinterpret_cast<const uint4*>(sm + kK + soff);
             const uint4 ukh = *reinterpret_cast<const uint4*>(sm + kK + 16384 + soff);
             const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
@@ -376,14 +379,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
             for (int e = 0; e < 4; ++e) {
               const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
               const float2 ns2 = f2(-sn[2 * e], -sn[2 * e + 1]);
-              const float2 ulo = add2(bf2f(ql[e]), *reinterpret_cast<const float2*>(qbp + 2 * e));
-              const float2 uhi = add2(bf2f(qh[e]), *reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
               const float2 wlo = add2(bf2f(kl[e]), *reinterpret_cast<const float2*>(kbp + 2 * e));
               const float2 whi = add2(bf2f(kh[e]), *reinterpret_cast<const float2*>(kbp + 64 + 2 * e));
-              uw2 = fma2(ulo, wlo, uw2);
-              uw2 = fma2(uhi, whi, uw2);
-              pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
-              pq_hi[e] = f2bf(fma2(ulo, s2, mul2(uhi, c2)));
+              if constexpr (!STATES) {
+                const float2 ulo = add2(bf2f(ql[e]), *reinterpret_cast<const float2*>(qbp + 2 * e));
+                const float2 uhi = add2(bf2f(qh[e]), *reinterpret_cast<const float2*>(qbp + 64 + 2 * e));
+                uw2 = fma2(ulo, wlo, uw2);
+                uw2 = fma2(uhi, whi, uw2);
+                pq_lo[e] = f2bf(fma2(uhi, ns2, mul2(ulo, c2)));
+                pq_hi[e] = f2bf(fma2(ulo, s2, mul2(uhi, c2)));
+              }
               const float2 klo = fma2(whi, ns2, mul2(wlo, c2));
               const float2 khi = fma2(wlo, s2, mul2(whi, c2));
               if (tgl == L - 1 && a.final_k) {  // final k is rotated but unscaled (kernel_fwd.py:192-201)
@@ -396,12 +401,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
               pk_lo[e] = f2bf(mul2(klo, f2s(sc)));
               pk_hi[e] = f2bf(mul2(khi, f2s(sc)));
             }
-            const float uw = uw2.x + uw2.y;
-            *reinterpret_cast<uint4*>(sm + kQ + soff) = make_uint4(pq_lo[0], pq_lo[1], pq_lo[2], pq_lo[3]);
-            *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = make_uint4(pq_hi[0], pq_hi[1], pq_hi[2], pq_hi[3]);
+            if constexpr (!STATES) {
+              *reinterpret_cast<uint4*>(sm + kQ + soff) = make_uint4(pq_lo[0], pq_lo[1], pq_lo[2], pq_lo[3]);
+              *reinterpret_cast<uint4*>(sm + kQ + 16384 + soff) = make_uint4(pq_hi[0], pq_hi[1], pq_hi[2], pq_hi[3]);
+              uws[g * 128 + tt] = uw2.x + uw2.y;
+            }
             *reinterpret_cast<uint4*>(sm + kK + soff) = make_uint4(pk_lo[0], pk_lo[1], pk_lo[2], pk_lo[3]);
             *reinterpret_cast<uint4*>(sm + kK + 16384 + soff) = make_uint4(pk_hi[0], pk_hi[1], pk_hi[2], pk_hi[3]);
-            uws[g * 128 + tt] = uw;
           }
         }
         if (RAW)
@@ -410,8 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       }
       M3_TC_MARK(1);
       slot_sync(slot);
-      float dg;
-      {
+      float dg = 0.f;
+      if constexpr (!STATES) {
         const float* uws = reinterpret_cast<const float*>(sm + kVd + kScrUw);
         float uw = 0.f;
 #pragma unroll
