@@ -34,7 +34,7 @@ __device__ __forceinline__ void expect_tx(uint64_t* mbar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(umma::smem_u32(mbar)), "r"(bytes)
                : "memory");
 }
-// global -> shared, completion counted on `mbar` (no multicast)
+// global -> shared of this CTA, completion counted on `mbar`
 __device__ __forceinline__ void load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* mbar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    umma::smem_u32(smem_dst)),
