@@ -257,26 +257,23 @@ def bench_fwd(c, steps, warmup, world, rank, peaks):
 
 
 def bench_e2e(c, steps, warmup, world, rank):
-    """Public API with pinned host buffers: H2D of every input, the forward, D2H of y."""
+    """Public API with pinned host buffers: H2D of every input, the forward, D2H of y, each
+    step (`siso.siso_segment_streamed`)."""
     from mamba3_b200 import siso as S
 
     d = make_cfg2_inputs(c, seed=2000 + rank)
     names = ["q", "k", "x", "z", "dt_raw", "a_raw", "trap_raw", "angles"]
     host = {n: d[n].cpu().pin_memory() for n in names}
-    dev = {n: torch.empty_like(d[n]) for n in names}
     small = {n: d[n] for n in ("dt_bias", "q_bias", "k_bias", "d_skip")}
     y_host = torch.empty(c["B"], c["L"], c["H"], c["P"], dtype=torch.bfloat16).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = y_host.numel() * y_host.element_size()
 
     def step():
-        for n in names:
-            dev[n].copy_(host[n], non_blocking=True)
-        out = S.siso_segment(dev["q"], dev["k"], dev["x"].permute(0, 2, 1, 3), dev["dt_raw"], dev["a_raw"],
-                             dev["trap_raw"], dev["angles"], small["dt_bias"], small["q_bias"], small["k_bias"],
-                             small["d_skip"], dev["z"].permute(0, 2, 1, 3), chunk=c["chunk"], policy_name="bf16",
-                             y_blhp=True)
-        y_host.copy_(out.y.permute(0, 2, 1, 3), non_blocking=True)
+        # host -> device, the scan and device -> host overlap over 8 segments of L
+        S.siso_segment_streamed(host["q"], host["k"], host["x"], host["dt_raw"], host["a_raw"], host["trap_raw"],
+                                host["angles"], small["dt_bias"], small["q_bias"], small["k_bias"], small["d_skip"],
+                                host["z"], chunk=c["chunk"], policy_name="bf16", segments=8, y_out=y_host)
 
     with torch.no_grad():
         ms = timed(step, steps, warmup, world)

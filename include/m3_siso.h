@@ -203,6 +203,13 @@ int m3_siso_decode(const M3DecodeArgs *args, void *stream);
  * the device.  `reset` != 0 clears it. */
 int m3_device_error(int reset);
 
+/* Host plumbing for callers that stream host buffers through the scan in pieces (no
+ * counterpart in the reference, whose inputs are device arrays): `height` rows of `width`
+ * bytes, row pitches `dpitch` / `spitch`, between any host (pinned) and device pointers,
+ * asynchronous on `stream`.  One strided copy moves an L-segment of every batch row. */
+int m3_copy2d_async(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t height,
+                    void *stream);
+
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);
 

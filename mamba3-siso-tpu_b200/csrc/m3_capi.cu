@@ -95,6 +95,17 @@ const char* m3_last_error(void) { return g_err.c_str(); }
 
 int m3_version(void) { return 1; }
 
+int m3_copy2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,
+                    void* stream) {
+  if (!dst || !src) return m3::set_error(M3_ERR_ARG, "m3_copy2d_async: NULL pointer");
+  if (width > dpitch || width > spitch) return m3::set_error(M3_ERR_SHAPE, "m3_copy2d_async: width exceeds a pitch");
+  if (width == 0 || height == 0) return M3_OK;
+  const cudaError_t e =
+      cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDefault, (cudaStream_t)stream);
+  if (e != cudaSuccess) return m3::set_error(M3_ERR_LAUNCH, std::string("m3_copy2d_async: ") + cudaGetErrorString(e));
+  return M3_OK;
+}
+
 int m3_device_error(int reset) {
   const int f = read_device_error(reset), d = read_decode_error(reset);
   return f != 0 ? f : d;

@@ -100,7 +100,7 @@ class M3DecodeArgs(ctypes.Structure):
 
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
-           "m3_device_error")
+           "m3_device_error", "m3_copy2d_async")
 
 _lib = None
 
@@ -128,6 +128,8 @@ def lib():
         L.m3_version.restype = ctypes.c_int
         L.m3_device_error.argtypes = [ctypes.c_int]
         L.m3_device_error.restype = ctypes.c_int
+        L.m3_copy2d_async.argtypes = [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]
+        L.m3_copy2d_async.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -132,3 +132,74 @@ def siso_segment(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bi
     y, fs, fk, fv, fphi = _SegmentFn.apply(q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias,
                                            d_skip, sp, sk, sv, sphi, a_floor, chunk, policy_name, y_blhp)
     return SISOOutput(y=y, state=SISOState(ssm=fs, k=fk, v=fv, phi=fphi))
+
+
+def siso_segment_streamed(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=None, z=None,
+                          a_floor: float = 1e-4, chunk: int = 128, policy_name: str = "bf16",
+                          segments: int = 8, y_out: Optional[torch.Tensor] = None) -> SISOOutput:
+    """`siso_segment` over inputs that live in pinned host memory, with y written back to host.
+
+    Layouts are the in_proj ones: q, k ``(B,L,N)``; v, z ``(B,L,H,P)``; raw dt / A / trap
+    ``(B,L,H)``; angles ``(B,L,Nr)``; the per-head parameters are device tensors.  The
+    sequence is cut into ``segments`` pieces along L (each a multiple of ``chunk``), scanned
+    one after another with the state carried (the segmentation rule of ``siso.py:176-181``),
+    while the next piece's inputs go host -> device and the previous piece's y goes device
+    -> host on two side streams.  Returns ``SISOOutput(y_host (B,L,H,P), final state on the
+    device)``; the caller's current stream is ordered after everything.  Forward only.
+    """
+    from . import _capi as C
+
+    B, L = q.shape[0], q.shape[1]
+    H, P = v.shape[2], v.shape[3]
+
+    def rows_copy(dst, src, t0, n_tok, d_t0, stream):
+        # tokens [t0, t0 + n_tok) of every batch row of src -> tokens [d_t0, ...) of dst, one
+        # strided copy (both (B, L, ...) with contiguous rows)
+        es = src.element_size()
+        tok = src[0, 0].numel() * es
+        if src.stride(1) * es != tok or dst.stride(1) * es != tok:
+            raise ValueError("siso_segment_streamed: every batch row must be token-contiguous")
+        C.check(C.lib().m3_copy2d_async(dst.data_ptr() + d_t0 * tok, dst.stride(0) * es, src.data_ptr() + t0 * tok,
+                                        src.stride(0) * es, n_tok * tok, src.shape[0], stream.cuda_stream))
+
+    seg = max(chunk, (L // max(segments, 1)) // chunk * chunk)
+    while L % seg:
+        seg -= chunk
+    n_seg = L // seg
+    cur = torch.cuda.current_stream()
+    dev = q.device if q.is_cuda else dt_bias.device
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_in.wait_stream(cur)  # the device buffers below may reuse memory the current stream still reads
+    names = ("q", "k", "v", "z", "dt_raw", "a_raw", "trap_raw", "angles")
+    host = dict(q=q, k=k, v=v, z=z, dt_raw=dt_raw, a_raw=a_raw, trap_raw=trap_raw, angles=angles)
+    dbuf = {n: torch.empty(t.shape, dtype=t.dtype, device=dev) for n, t in host.items() if t is not None}
+    if y_out is None:
+        y_out = torch.empty(B, L, H, P, dtype=v.dtype, pin_memory=True)
+    state = None
+    keep = []
+    with torch.no_grad():
+        for i in range(n_seg):
+            sl = slice(i * seg, (i + 1) * seg)
+            for n in names:
+                if host[n] is not None:
+                    rows_copy(dbuf[n], host[n], i * seg, seg, i * seg, s_in)
+            ev_in = torch.cuda.Event()
+            ev_in.record(s_in)
+            cur.wait_event(ev_in)
+            out = siso_segment(dbuf["q"][:, sl], dbuf["k"][:, sl], dbuf["v"][:, sl].permute(0, 2, 1, 3),
+                               dbuf["dt_raw"][:, sl], dbuf["a_raw"][:, sl], dbuf["trap_raw"][:, sl],
+                               dbuf["angles"][:, sl], dt_bias, q_bias, k_bias, d_skip,
+                               None if z is None else dbuf["z"][:, sl].permute(0, 2, 1, 3), state=state,
+                               a_floor=a_floor, chunk=chunk, policy_name=policy_name, y_blhp=True)
+            state = out.state
+            ybuf = out.y.permute(0, 2, 1, 3)  # (B, seg, H, P), contiguous
+            ev_c = torch.cuda.Event()
+            ev_c.record(cur)
+            s_out.wait_event(ev_c)
+            ybuf.record_stream(s_out)
+            rows_copy(y_out, ybuf, 0, seg, i * seg, s_out)
+            keep.append(ybuf)
+    for t in dbuf.values():
+        t.record_stream(s_in)
+    cur.wait_stream(s_out)
+    return SISOOutput(y=y_out, state=state)
