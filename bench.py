@@ -303,7 +303,7 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
     th = c["B"] * c["L"] * c["H"]
     flops = (FWD_FLOP_PER_TOKEN_HEAD + BWD_FLOP_PER_TOKEN_HEAD) * th
     return {"tok_s": c["B"] * c["L"] * world / (per / 1e3), "ms_per_step": per,
-            "tflops": flops / (per / 1e3) / 1e12, "launches_per_step": 2}
+            "tflops": flops / (per / 1e3) / 1e12, "launches_per_step": 3}  # fwd, states sweep, bwd
 
 
 def bench_decode(steps, warmup, world, rank, peaks, batch=256):
