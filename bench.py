@@ -306,6 +306,61 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
             "tflops": flops / (per / 1e3) / 1e12, "launches_per_step": 3}  # fwd, states sweep, bwd
 
 
+def markov3_tokens(batch, length, seed, device="cuda", vocab=256, alpha=0.1):
+    """Seeded order-3 Markov source over 256 symbols with Dirichlet(alpha) transition rows
+    (configs[4]'s stand-in for a byte corpus).  The 256^3 rows are never materialised: the
+    row of context c is the normalised Gamma(alpha) draws of a counter-based hash of
+    (seed, c, symbol), and the next symbol is drawn by Gumbel-max over its logarithms."""
+    M64 = (1 << 63) - 1
+
+    def mix(x):  # splitmix-style integer hash on int64 (arithmetic wraps)
+        x = (x ^ (x >> 31)) * 0x5851F42D4C957F2D
+        x = (x ^ (x >> 29)) * 0x14057B7EF767814F
+        return (x ^ (x >> 32)) & M64
+
+    def unif(x):
+        return ((mix(x) >> 11).double() + 0.5) / float(1 << 52)
+
+    sym = torch.arange(vocab, device=device, dtype=torch.int64)
+    g = torch.Generator(device=device).manual_seed(seed)
+    toks = torch.empty(batch, length, dtype=torch.int64, device=device)
+    ctx = torch.randint(0, vocab ** 3, (batch,), device=device, generator=g)
+    for t in range(length):
+        key = (ctx[:, None] * vocab + sym[None, :]) * 0x9E3779B97F4A7C15 + seed
+        # Gamma(alpha) draw for alpha < 1 via U^(1/alpha) * Gamma(1 + alpha) ~ U^(1/alpha) * Exp(1)
+        logw = torch.log(unif(key)) / alpha + torch.log(-torch.log(unif(key + 0x632BE59BD9B4E019)))
+        gumbel = -torch.log(-torch.log(torch.rand(batch, vocab, device=device, generator=g, dtype=torch.float64)))
+        nxt = torch.argmax(logw + gumbel, dim=1)
+        toks[:, t] = nxt
+        ctx = (ctx * vocab + nxt) % (vocab ** 3)
+    return toks
+
+
+def bench_train(steps, warmup, world, rank, global_batch=64, seq_len=8192):
+    """data-parallel training of the 8-layer byte-level LM (d_model 512, N 128,
+    P 64, H 16, Nr 32, chunk 128, tied head, no MLP), bf16 compute on fp32 master weights,
+    AdamW lr 1e-3, NCCL all-reduce of bucketed gradients.  The global batch of 64 x 8192 is
+    split over the ranks (strong scaling); tokens come from `markov3_tokens`."""
+    from mamba3_b200 import layer as LY
+    from mamba3_b200 import model as M
+    from mamba3_b200 import train as T
+
+    per = max(1, global_batch // world)
+    scfg = LY.SISOConfig(d_model=512, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                         policy_name="bf16")
+    cfg = M.LMConfig(vocab_size=256, n_layers=8, siso=scfg, d_intermediate=0)
+    params = M.init_lm(cfg, key=0, dtype=torch.float32)
+    step = T.make_step(cfg, params, lr=1e-3)
+    toks = markov3_tokens(per, seq_len + 1, seed=5000 + rank)
+    xs, ys = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
+    ms = timed(lambda: step(xs, ys), steps, warmup, world)
+    t = ms / steps
+    loss = float(step(xs, ys))
+    return {"tok_s": per * world * seq_len / (t / 1e3), "ms_per_step": t, "global_batch": per * world,
+            "seq_len": seq_len, "params": cfg.param_count(), "loss": loss, "scaling": "strong (global batch 64)",
+            "data": "synthetic order-3 Markov bytes, Dirichlet(0.1) rows"}
+
+
 def bench_decode(steps, warmup, world, rank, peaks, batch=256):
     """24-layer LM, d_model 2048, N 128, P 64, H 64, Nr 32, MLP 4096,
     vocab 128256, bf16 weights, B=256 (per rank), state pre-filled by a 512-token prefill."""
@@ -458,7 +513,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,cpu or all")
+    ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,cpu or all")
     ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
@@ -472,7 +527,7 @@ def main():
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
-    what = set(["fwd", "e2e", "fwdbwd", "decode", "cpu"] if args.what == "all" else args.what.split(","))
+    what = set(["fwd", "e2e", "fwdbwd", "decode", "train", "cpu"] if args.what == "all" else args.what.split(","))
     peaks = load_peaks()
     traffic = load_traffic()
     c = dict(CFG2)
@@ -486,6 +541,8 @@ def main():
             out["fwd_bwd"] = bench_fwd_bwd(c, max(2, args.steps // 2), args.warmup, world, rank)
         if "decode" in what:
             out["decode"] = bench_decode(args.steps, args.warmup, world, rank, peaks)
+        if "train" in what:
+            out["train"] = bench_train(max(2, args.steps // 3), args.warmup, world, rank)
     clocks = clk.summary()
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
 
@@ -529,6 +586,8 @@ def main():
         line["fwd_bwd"] = out["fwd_bwd"]
     if "decode" in out:
         line["decode"] = out["decode"]
+    if "train" in out:
+        line["train"] = out["train"]
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
