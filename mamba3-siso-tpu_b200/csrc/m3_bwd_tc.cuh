@@ -185,6 +185,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma::cp_async16(aV + umma::sw128_off(row, c8),
                        v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h + (size_t)(tb + row) * a.v_st.l + c8 * 8);
     }
+    // dy into the g tile (g is computed in place) and z into the vd tile (free until P2)
+    const __nv_bfloat16* dyb = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tb * a.dy_st.l;
+    const __nv_bfloat16* zb = z ? z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tb * a.z_st.l : nullptr;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i = tid + kThreads * m;
+      const int row = i >> 3, c8 = i & 7;
+      umma::cp_async16(aG + umma::sw128_off(row, c8), dyb + (size_t)row * a.dy_st.l + c8 * 8);
+      if (zb) umma::cp_async16(aVd + umma::sw128_off(row, c8), zb + (size_t)row * a.z_st.l + c8 * 8);
+    }
     const int n4 = Nr >> 2;  // 16-byte chunks per angle row
     const uint32_t aAng = umma::smem_u32(sm + kAng);
     for (int i = tid; i < kC * n4; i += kThreads) {
@@ -238,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<float*>(sm + kScrDt)[t] = dt;
       reinterpret_cast<float*>(sm + kScrScl)[t] = scl;
     }
+    umma::cp_async_wait_all();  // this chunk's prefetched tiles (dy / z included)
     __syncthreads();
     float A = incl;
     for (int w = 0; w < (warp & 3); ++w) A += ss->wtot[w];
@@ -247,22 +258,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // g = dy silu(z) for this thread's 32 columns; bf16 g and e^A g tiles (rows = token)
     float gv[32];
     {
-      const __nv_bfloat16* dyr = dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)tg * a.dy_st.l + 32 * half;
-      const __nv_bfloat16* zr = z ? z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)tg * a.z_st.l + 32 * half
-                                  : nullptr;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint4 u = *reinterpret_cast<const uint4*>(dyr + 8 * j);
+        const uint32_t so = umma::sw128_off(t, 4 * half + j);
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + kG + so);
         const uint32_t d4[4] = {u.x, u.y, u.z, u.w};
         uint32_t z4[4] = {0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u};
-        if (zr) {
-          const uint4 w = *reinterpret_cast<const uint4*>(zr + 8 * j);
+        if (z) {
+          const uint4 w = *reinterpret_cast<const uint4*>(sm + kVd + so);
           z4[0] = w.x; z4[1] = w.y; z4[2] = w.z; z4[3] = w.w;
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float2 g2 = bf2f(d4[e]);
-          if (zr) {
+          if (z) {
             const float2 z2 = bf2f(z4[e]);
             g2 = mul2(g2, mul2(z2, sigmoid2(z2)));
           }
