@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* dst = (mat ? a.dk : a.dq) + ((size_t)b * L + t0) * kN + 4 * lane;
 #pragma unroll 4
       for (int rr = 0; rr < 32; ++rr) {
-        const int tt = 32 * (warp & 3) + rr;
+        const int tt = 32 * (warp & 3) + ((rr + 5 * h) & 31);  // heads start on different rows
         const float4 v = *reinterpret_cast<const float4*>(src + tt * 128 + 4 * (lane ^ (tt & 7)));
         bias01 = add2(bias01, f2(v.x, v.y));
         bias23 = add2(bias23, f2(v.z, v.w));
