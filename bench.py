@@ -306,6 +306,21 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
             "tflops": flops / (per / 1e3) / 1e12, "launches_per_step": 3}  # fwd, states sweep, bwd
 
 
+def bench_layer_cfg0(steps, warmup, world):
+    """one Mamba-3 SISO layer forward in fp32 (d_model 256, N 32, P 32, H 16,
+    Nr 8, chunk 64) on u (2, 512, 256) ~ N(0, 1), parameters from `init_params(seed 0)`.
+    Parity with the reference is a test (tests/test_model_gpu.py); this is the wall time."""
+    from mamba3_b200 import layer as LY
+
+    cfg = LY.SISOConfig(d_model=256, d_state=32, headdim=32, expand=2, rope_fraction=0.5, chunk=64,
+                        policy_name="fp32")
+    params = LY.init_params(cfg, key=0, dtype=torch.float32)
+    u = torch.randn(2, 512, 256, generator=torch.Generator().manual_seed(1)).cuda()
+    with torch.no_grad():
+        ms = timed(lambda: LY.mamba3_siso_layer(params, u, cfg), steps, warmup, world)
+    return {"ms_per_forward": ms / steps, "shape": "u (2, 512, 256), fp32 policy", "kernel": "generic (fp32)"}
+
+
 def markov3_tokens(batch, length, seed, device="cuda", vocab=256, alpha=0.1):
     """Seeded order-3 Markov source over 256 symbols with Dirichlet(alpha) transition rows
     (configs[4]'s stand-in for a byte corpus).  The 256^3 rows are never materialised: the
@@ -513,7 +528,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,cpu or all")
+    ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu or all")
     ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
@@ -527,7 +542,8 @@ def main():
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
-    what = set(["fwd", "e2e", "fwdbwd", "decode", "train", "cpu"] if args.what == "all" else args.what.split(","))
+    what = set(["fwd", "e2e", "fwdbwd", "decode", "train", "layer", "cpu"] if args.what == "all"
+               else args.what.split(","))
     peaks = load_peaks()
     traffic = load_traffic()
     c = dict(CFG2)
@@ -543,6 +559,8 @@ def main():
             out["decode"] = bench_decode(args.steps, args.warmup, world, rank, peaks)
         if "train" in what:
             out["train"] = bench_train(max(2, args.steps // 3), args.warmup, world, rank)
+        if "layer" in what:
+            out["layer_cfg0"] = bench_layer_cfg0(args.steps, args.warmup, world)
     clocks = clk.summary()
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
 
@@ -588,6 +606,8 @@ def main():
         line["decode"] = out["decode"]
     if "train" in out:
         line["train"] = out["train"]
+    if "layer_cfg0" in out:
+        line["layer_cfg0"] = out["layer_cfg0"]
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
