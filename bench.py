@@ -489,6 +489,25 @@ def run_profile_case(which):
     """Three launches of one path on a case small enough for a full ncu capture.  Its inputs
     (v, z, y 67 MB each at L = 2048) are still larger than L2."""
     torch.cuda.set_device(0)
+    if which == "decodestep":  # configs[3]: one 24-layer decode step, eager, inside an NVTX range
+        from mamba3_b200 import layer as LY
+        from mamba3_b200 import model as M
+
+        scfg = LY.SISOConfig(d_model=2048, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                             policy_name="bf16")
+        cfg = M.LMConfig(vocab_size=128256, n_layers=24, siso=scfg, d_intermediate=4096)
+        params = M.init_lm(cfg, key=0, dtype=torch.bfloat16)
+        states = M.zero_states(cfg, 256)
+        tok = torch.randint(0, cfg.vocab_size, (256,), device="cuda")
+        with torch.no_grad():
+            for i in range(3):
+                if i == 2:
+                    torch.cuda.nvtx.range_push("decode_step")
+                M.lm_decode_step(params, tok, states, cfg)
+                if i == 2:
+                    torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        return 0
     if which == "decode":
         from mamba3_b200 import kernel_decode as KD
         from mamba3_b200.state import SISOState
@@ -529,7 +548,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode"],
+    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()

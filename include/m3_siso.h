@@ -210,6 +210,13 @@ int m3_device_error(int reset);
 int m3_copy2d_async(void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t height,
                     void *stream);
 
+/* RMS normalisation of `rows` rows of `dim` elements (layer.py:190-198):
+ * y = x * rsqrt(mean(x^2) + eps) * weight, computed in fp32 and stored in x's dtype.  Row
+ * strides in elements; x / y dtype and weight dtype are M3_DTYPE_*.  The decode and
+ * inference paths' block, B / C and final norms. */
+int m3_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *y, int64_t y_row_stride, int64_t rows,
+                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, void *stream);
+
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);
 

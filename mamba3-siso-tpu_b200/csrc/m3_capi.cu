@@ -95,6 +95,18 @@ const char* m3_last_error(void) { return g_err.c_str(); }
 
 int m3_version(void) { return 1; }
 
+int m3_rms_norm(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t y_row_stride, int64_t rows,
+                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, void* stream) {
+  if (!x || !weight || !y) return m3::set_error(M3_ERR_ARG, "m3_rms_norm: NULL pointer");
+  if (rows < 0 || dim <= 0 || x_row_stride < dim || y_row_stride < dim)
+    return m3::set_error(M3_ERR_SHAPE, "m3_rms_norm: bad rows / dim / strides");
+  if ((x_dtype != M3_DTYPE_BF16 && x_dtype != M3_DTYPE_F32) || (w_dtype != M3_DTYPE_BF16 && w_dtype != M3_DTYPE_F32))
+    return m3::set_error(M3_ERR_UNSUPPORTED, "m3_rms_norm: dtype must be bf16 or f32");
+  if (rows == 0) return M3_OK;
+  return m3::launch_rms_norm(x, x_row_stride, weight, y, y_row_stride, rows, dim, eps, x_dtype, w_dtype,
+                             (cudaStream_t)stream);
+}
+
 int m3_copy2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,
                     void* stream) {
   if (!dst || !src) return m3::set_error(M3_ERR_ARG, "m3_copy2d_async: NULL pointer");

@@ -20,6 +20,8 @@ bool supported_np(int n, int p);
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s);
 int read_device_error(int reset);
 int read_decode_error(int reset);
+int launch_rms_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
+                    int x_dtype, int w_dtype, cudaStream_t s);
 int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s);
 bool fwd_tc_eligible_public(const M3FwdArgs& a);
 size_t bwd_tc_workspace_bytes(const M3Dims& d);

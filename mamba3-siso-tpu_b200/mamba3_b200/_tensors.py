@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import _capi as C
@@ -49,8 +51,27 @@ def f32c(t):
     return t
 
 
+_F32_CACHE = {}  # id(tensor) -> (weakref to it, its version, fp32 copy); tensors compare elementwise, so no WeakKeyDictionary
+
+
 def f32dense(t):
-    return None if t is None else t.float().contiguous()
+    """fp32, dense.  Small tensors that need a conversion (per-head parameters held in bf16)
+    are converted once and reused while their version is unchanged, so a decode step does
+    not re-convert every layer's biases on every token."""
+    if t is None:
+        return None
+    if t.dtype == torch.float32 and t.is_contiguous():
+        return t
+    if t.numel() <= (1 << 16) and not t.requires_grad:
+        key = id(t)
+        hit = _F32_CACHE.get(key)
+        if hit is not None and hit[0]() is t and hit[1] == t._version:
+            return hit[2]
+        c = t.float().contiguous()
+        if not (t.is_cuda and torch.cuda.is_current_stream_capturing()):
+            _F32_CACHE[key] = (weakref.ref(t, lambda _r, k=key: _F32_CACHE.pop(k, None)), t._version, c)
+        return c
+    return t.float().contiguous()
 
 
 def inner_contig(t, dtype):

@@ -130,10 +130,41 @@ def split_in_proj(proj: torch.Tensor, cfg: SISOConfig):
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-    """``layer.py:190-198``: f32 internally, gain after scaling, cast back."""
+    """``layer.py:190-198``: f32 internally, gain after scaling, cast back.
+
+    Without autograd (decode, inference) one fused kernel (`m3_rms_norm`) does it; with
+    autograd the torch ops below do, so that their backward exists."""
+    if _fused_norm_ok(x, weight):
+        return _rms_norm_fused(x, weight, eps)
     xf = x.float()
     rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return (xf * rstd * weight.float()).to(x.dtype)
+
+
+def _fused_norm_ok(x, weight) -> bool:
+    if not (x.is_cuda and weight.is_cuda) or x.dim() < 1 or x.stride(-1) != 1 or weight.dim() != 1:
+        return False
+    if x.dtype not in (torch.bfloat16, torch.float32) or weight.dtype not in (torch.bfloat16, torch.float32):
+        return False
+    if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad):
+        return False
+    if x.dim() > 2 and not x.is_contiguous():
+        return False
+    return weight.is_contiguous() and weight.shape[0] == x.shape[-1]
+
+
+def _rms_norm_fused(x, weight, eps):
+    from . import _capi as C
+    from . import _tensors as T
+
+    dim = x.shape[-1]
+    rows = x.numel() // dim if dim else 0
+    x_stride = x.stride(0) if x.dim() == 2 else dim
+    y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    code = lambda t: C.M3_DTYPE_BF16 if t.dtype == torch.bfloat16 else C.M3_DTYPE_F32
+    C.check(C.lib().m3_rms_norm(T.ptr(x), x_stride, T.ptr(weight), T.ptr(y), dim, rows, dim, float(eps), code(x),
+                                code(weight), T.stream_handle(x.device)))
+    return y
 
 
 def _scalar_streams(proj: torch.Tensor, cfg: SISOConfig):
