@@ -1,6 +1,6 @@
 // Fused RMS normalisation of rows (layer.py:190-198, model.py's block / final norms):
 //   y = x * rsqrt(mean(x^2) + eps) * w      in fp32, stored in x's dtype.
-// One warp per row: a pass for the sum of squares (16-byte vectors when the row allows),
+// One warp (or four, for rows of 1024+) per row: a pass for the sum of squares (16-byte vectors when the row allows),
 // a warp reduction, and a pass that scales (the row is back from L1 / L2).  Replaces the
 // seven elementwise / reduction launches of the unfused form in the decode and inference
 // paths.
@@ -9,70 +9,87 @@
 
 namespace m3 {
 
-constexpr int kNormThreads = 256, kNormRowsPerCta = kNormThreads / 32;
+constexpr int kNormThreads = 256;
 
-template <typename T>
-__device__ __forceinline__ float ldf(const T* p) {
-  return ld(p);
-}
-
-template <typename T, typename W, bool VEC>
+// TPR threads per row (32: one warp; 128: four warps joined through shared memory, for
+// long rows, so that a few hundred rows still fill the GPU).
+template <typename T, typename W, bool VEC, int TPR>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restrict__ x, int64_t xs,
                                                                 const W* __restrict__ w, T* __restrict__ y, int64_t ys,
                                                                 int64_t rows, int dim, float eps) {
-  const int64_t row = (int64_t)blockIdx.x * kNormRowsPerCta + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  constexpr int RPC = kNormThreads / TPR;  // rows per CTA
+  __shared__ float part[kNormThreads / 32];
+  const int sub = threadIdx.x % TPR;      // this thread's index within its row
+  const int64_t row = (int64_t)blockIdx.x * RPC + threadIdx.x / TPR;
+  const bool live = row < rows;
   const T* xr = x + row * xs;
   T* yr = y + row * ys;
   constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
   float ss = 0.f;
-  if (VEC) {
-    for (int i = lane * V; i < dim; i += 32 * V) {
-      const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
-      const T* e = reinterpret_cast<const T*>(&u);
+  if (live) {
+    if (VEC) {
+      for (int i = sub * V; i < dim; i += TPR * V) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
+        const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
-      for (int j = 0; j < V; ++j) {
-        const float f = ld(e + j);
+        for (int j = 0; j < V; ++j) {
+          const float f = ld(e + j);
+          ss = fmaf(f, f, ss);
+        }
+      }
+    } else {
+      for (int i = sub; i < dim; i += TPR) {
+        const float f = ld(xr + i);
         ss = fmaf(f, f, ss);
       }
     }
-  } else {
-    for (int i = lane; i < dim; i += 32) {
-      const float f = ld(xr + i);
-      ss = fmaf(f, f, ss);
-    }
   }
   ss = warp_sum(ss);
+  if (TPR > 32) {
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    const int w0 = (threadIdx.x / TPR) * (TPR / 32);
+    ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < TPR / 32; ++k) ss += part[w0 + k];
+  }
+  if (!live) return;
   const float r = rsqrtf(ss / (float)dim + eps);
   if (VEC) {
-    for (int i = lane * V; i < dim; i += 32 * V) {
+    for (int i = sub * V; i < dim; i += TPR * V) {
       const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
       const T* e = reinterpret_cast<const T*>(&u);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int j = 0; j < V; ++j) stg<T>(oe + j, ld(e + j) * r * ldf(w + i + j));
+      for (int j = 0; j < V; ++j) stg<T>(oe + j, ld(e + j) * r * ld(w + i + j));
       *reinterpret_cast<uint4*>(yr + i) = o;
     }
   } else {
-    for (int i = lane; i < dim; i += 32) stg<T>(yr + i, ld(xr + i) * r * ldf(w + i));
+    for (int i = sub; i < dim; i += TPR) stg<T>(yr + i, ld(xr + i) * r * ld(w + i));
   }
+}
+
+template <typename T, typename W, int TPR>
+static int run_norm_t(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
+                      cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T), RPC = kNormThreads / TPR;
+  const bool vec = dim % V == 0 && xs % V == 0 && ys % V == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0;
+  const int64_t grid = (rows + RPC - 1) / RPC;
+  if (vec)
+    rms_norm_kernel<T, W, true, TPR><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys,
+                                                                             rows, dim, eps);
+  else
+    rms_norm_kernel<T, W, false, TPR><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys,
+                                                                              rows, dim, eps);
+  return check_launch("m3_rms_norm");
 }
 
 template <typename T, typename W>
 static int run_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
                     cudaStream_t s) {
-  constexpr int V = 16 / sizeof(T);
-  const bool vec = dim % V == 0 && xs % V == 0 && ys % V == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0;
-  const int64_t grid = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
-  if (vec)
-    rms_norm_kernel<T, W, true><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys, rows,
-                                                                        dim, eps);
-  else
-    rms_norm_kernel<T, W, false><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys,
-                                                                         rows, dim, eps);
-  return check_launch("m3_rms_norm");
+  return dim >= 1024 ? run_norm_t<T, W, 128>(x, xs, w, y, ys, rows, dim, eps, s)
+                     : run_norm_t<T, W, 32>(x, xs, w, y, ys, rows, dim, eps, s);
 }
 
 int launch_rms_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
