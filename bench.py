@@ -489,6 +489,26 @@ def run_profile_case(which):
     """Three launches of one path on a case small enough for a full ncu capture.  Its inputs
     (v, z, y 67 MB each at L = 2048) are still larger than L2."""
     torch.cuda.set_device(0)
+    if which == "trainstep":  # configs[4]: one optimizer step at 1/8 of the global batch, inside an NVTX range
+        from mamba3_b200 import layer as LY
+        from mamba3_b200 import model as M
+        from mamba3_b200 import train as T
+
+        scfg = LY.SISOConfig(d_model=512, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                             policy_name="bf16")
+        cfg = M.LMConfig(vocab_size=256, n_layers=8, siso=scfg, d_intermediate=0)
+        params = M.init_lm(cfg, key=0, dtype=torch.float32)
+        step = T.make_step(cfg, params, lr=1e-3)
+        toks = torch.randint(0, 256, (8, 8193), device="cuda")
+        xs, ys = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
+        for i in range(3):
+            if i == 2:
+                torch.cuda.nvtx.range_push("train_step")
+            step(xs, ys)
+            if i == 2:
+                torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        return 0
     if which == "decodestep":  # configs[3]: one 24-layer decode step, eager, inside an NVTX range
         from mamba3_b200 import layer as LY
         from mamba3_b200 import model as M
@@ -548,7 +568,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep"],
+    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep", "trainstep"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()

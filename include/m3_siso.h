@@ -215,7 +215,14 @@ int m3_copy2d_async(void *dst, size_t dpitch, const void *src, size_t spitch, si
  * strides in elements; x / y dtype and weight dtype are M3_DTYPE_*.  The decode and
  * inference paths' block, B / C and final norms. */
 int m3_rms_norm(const void *x, int64_t x_row_stride, const void *weight, void *y, int64_t y_row_stride, int64_t rows,
-                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, void *stream);
+                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, float *rstd, void *stream);
+/* `rstd` (optional, `rows` floats) receives rsqrt(mean(x^2) + eps) per row for the backward:
+ * dx = r (dy o w) - x r^3 / dim sum(dy o w o x) (x's dtype, row stride dx_row_stride) and
+ * dweight += sum over rows of dy o x r (fp32, `dim` floats, accumulated: zero it first).
+ * dim <= 2048. */
+int m3_rms_norm_bwd(const void *x, int64_t x_row_stride, const void *weight, const float *rstd, const void *dy,
+                    int64_t dy_row_stride, void *dx, int64_t dx_row_stride, float *dweight, int64_t rows, int32_t dim,
+                    int32_t x_dtype, int32_t w_dtype, void *stream);
 
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);

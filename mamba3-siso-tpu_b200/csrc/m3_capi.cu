@@ -96,15 +96,28 @@ const char* m3_last_error(void) { return g_err.c_str(); }
 int m3_version(void) { return 1; }
 
 int m3_rms_norm(const void* x, int64_t x_row_stride, const void* weight, void* y, int64_t y_row_stride, int64_t rows,
-                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, void* stream) {
+                int32_t dim, float eps, int32_t x_dtype, int32_t w_dtype, float* rstd, void* stream) {
   if (!x || !weight || !y) return m3::set_error(M3_ERR_ARG, "m3_rms_norm: NULL pointer");
   if (rows < 0 || dim <= 0 || x_row_stride < dim || y_row_stride < dim)
     return m3::set_error(M3_ERR_SHAPE, "m3_rms_norm: bad rows / dim / strides");
   if ((x_dtype != M3_DTYPE_BF16 && x_dtype != M3_DTYPE_F32) || (w_dtype != M3_DTYPE_BF16 && w_dtype != M3_DTYPE_F32))
     return m3::set_error(M3_ERR_UNSUPPORTED, "m3_rms_norm: dtype must be bf16 or f32");
   if (rows == 0) return M3_OK;
-  return m3::launch_rms_norm(x, x_row_stride, weight, y, y_row_stride, rows, dim, eps, x_dtype, w_dtype,
+  return m3::launch_rms_norm(x, x_row_stride, weight, y, y_row_stride, rows, dim, eps, x_dtype, w_dtype, rstd,
                              (cudaStream_t)stream);
+}
+
+int m3_rms_norm_bwd(const void* x, int64_t x_row_stride, const void* weight, const float* rstd, const void* dy,
+                    int64_t dy_row_stride, void* dx, int64_t dx_row_stride, float* dweight, int64_t rows, int32_t dim,
+                    int32_t x_dtype, int32_t w_dtype, void* stream) {
+  if (!x || !weight || !rstd || !dy || !dx || !dweight) return m3::set_error(M3_ERR_ARG, "m3_rms_norm_bwd: NULL pointer");
+  if (rows < 0 || dim <= 0 || dim > 2048 || x_row_stride < dim || dy_row_stride < dim || dx_row_stride < dim)
+    return m3::set_error(M3_ERR_SHAPE, "m3_rms_norm_bwd: bad rows / dim (<= 2048) / strides");
+  if ((x_dtype != M3_DTYPE_BF16 && x_dtype != M3_DTYPE_F32) || (w_dtype != M3_DTYPE_BF16 && w_dtype != M3_DTYPE_F32))
+    return m3::set_error(M3_ERR_UNSUPPORTED, "m3_rms_norm_bwd: dtype must be bf16 or f32");
+  if (rows == 0) return M3_OK;
+  return m3::launch_rms_norm_bwd(x, x_row_stride, weight, rstd, dy, dy_row_stride, dx, dx_row_stride, dweight, rows,
+                                 dim, x_dtype, w_dtype, (cudaStream_t)stream);
 }
 
 int m3_copy2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,

@@ -21,7 +21,10 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s);
 int read_device_error(int reset);
 int read_decode_error(int reset);
 int launch_rms_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
-                    int x_dtype, int w_dtype, cudaStream_t s);
+                    int x_dtype, int w_dtype, float* rstd, cudaStream_t s);
+int launch_rms_norm_bwd(const void* x, int64_t xs, const void* w, const float* rstd, const void* dy, int64_t dys,
+                        void* dx, int64_t dxs, float* dw, int64_t rows, int dim, int x_dtype, int w_dtype,
+                        cudaStream_t s);
 int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s);
 bool fwd_tc_eligible_public(const M3FwdArgs& a);
 size_t bwd_tc_workspace_bytes(const M3Dims& d);

@@ -16,7 +16,8 @@ constexpr int kNormThreads = 256;
 template <typename T, typename W, bool VEC, int TPR>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restrict__ x, int64_t xs,
                                                                 const W* __restrict__ w, T* __restrict__ y, int64_t ys,
-                                                                int64_t rows, int dim, float eps) {
+                                                                int64_t rows, int dim, float eps,
+                                                                float* __restrict__ rstd_out) {
   constexpr int RPC = kNormThreads / TPR;  // rows per CTA
   __shared__ float part[kNormThreads / 32];
   const int sub = threadIdx.x % TPR;      // this thread's index within its row
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
   }
   if (!live) return;
   const float r = rsqrtf(ss / (float)dim + eps);
+  if (rstd_out && sub == 0) rstd_out[row] = r;
   if (VEC) {
     for (int i = sub * V; i < dim; i += TPR * V) {
       const uint4 u = *reinterpret_cast<const uint4*>(xr + i);
@@ -72,33 +74,113 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
 
 template <typename T, typename W, int TPR>
 static int run_norm_t(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
-                      cudaStream_t s) {
+                      float* rstd, cudaStream_t s) {
   constexpr int V = 16 / sizeof(T), RPC = kNormThreads / TPR;
   const bool vec = dim % V == 0 && xs % V == 0 && ys % V == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)y % 16) == 0;
   const int64_t grid = (rows + RPC - 1) / RPC;
   if (vec)
     rms_norm_kernel<T, W, true, TPR><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys,
-                                                                             rows, dim, eps);
+                                                                             rows, dim, eps, rstd);
   else
     rms_norm_kernel<T, W, false, TPR><<<(unsigned)grid, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, (T*)y, ys,
-                                                                              rows, dim, eps);
+                                                                              rows, dim, eps, rstd);
   return check_launch("m3_rms_norm");
 }
 
 template <typename T, typename W>
 static int run_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
-                    cudaStream_t s) {
-  return dim >= 1024 ? run_norm_t<T, W, 128>(x, xs, w, y, ys, rows, dim, eps, s)
-                     : run_norm_t<T, W, 32>(x, xs, w, y, ys, rows, dim, eps, s);
+                    float* rstd, cudaStream_t s) {
+  return dim >= 1024 ? run_norm_t<T, W, 128>(x, xs, w, y, ys, rows, dim, eps, rstd, s)
+                     : run_norm_t<T, W, 32>(x, xs, w, y, ys, rows, dim, eps, rstd, s);
 }
 
 int launch_rms_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
-                    int x_dtype, int w_dtype, cudaStream_t s) {
+                    int x_dtype, int w_dtype, float* rstd, cudaStream_t s) {
   const bool xb = x_dtype == M3_DTYPE_BF16, wb = w_dtype == M3_DTYPE_BF16;
-  if (xb) return wb ? run_norm<__nv_bfloat16, __nv_bfloat16>(x, xs, w, y, ys, rows, dim, eps, s)
-                    : run_norm<__nv_bfloat16, float>(x, xs, w, y, ys, rows, dim, eps, s);
-  return wb ? run_norm<float, __nv_bfloat16>(x, xs, w, y, ys, rows, dim, eps, s)
-            : run_norm<float, float>(x, xs, w, y, ys, rows, dim, eps, s);
+  if (xb) return wb ? run_norm<__nv_bfloat16, __nv_bfloat16>(x, xs, w, y, ys, rows, dim, eps, rstd, s)
+                    : run_norm<__nv_bfloat16, float>(x, xs, w, y, ys, rows, dim, eps, rstd, s);
+  return wb ? run_norm<float, __nv_bfloat16>(x, xs, w, y, ys, rows, dim, eps, rstd, s)
+            : run_norm<float, float>(x, xs, w, y, ys, rows, dim, eps, rstd, s);
+}
+
+// Backward of y = x r w, r = rsqrt(mean(x^2) + eps), per row with g = dy o w:
+//   dx = r g - x (r^3 / dim) sum(g o x)         dw = sum over rows of dy o x r
+// One warp per row, rows strided over a persistent grid; each lane keeps its COLS columns'
+// dw partial sums in registers (dim <= 32 COLS) and adds them to dw once per CTA.
+template <typename T, typename W, int COLS>
+__global__ void __launch_bounds__(kNormThreads) rms_norm_bwd_kernel(const T* __restrict__ x, int64_t xs,
+                                                                    const W* __restrict__ w, const float* __restrict__ rstd,
+                                                                    const T* __restrict__ dy, int64_t dys,
+                                                                    T* __restrict__ dx, int64_t dxs,
+                                                                    float* __restrict__ dw, int64_t rows, int dim) {
+  __shared__ float dws[COLS * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) dws[i] = 0.f;
+  __syncthreads();
+  float acc[COLS];
+#pragma unroll
+  for (int j = 0; j < COLS; ++j) acc[j] = 0.f;
+  for (int64_t row = (int64_t)blockIdx.x * (kNormThreads / 32) + warp; row < rows;
+       row += (int64_t)gridDim.x * (kNormThreads / 32)) {
+    const T* xr = x + row * xs;
+    const T* gr = dy + row * dys;
+    const float r = rstd[row];
+    float sgx = 0.f;
+#pragma unroll
+    for (int j = 0; j < COLS; ++j) {
+      const int i = lane + 32 * j;
+      if (i < dim) sgx = fmaf(ld(gr + i) * ld(w + i), ld(xr + i), sgx);
+    }
+    sgx = warp_sum(sgx);
+    const float c = r * r * r * sgx / (float)dim;
+#pragma unroll
+    for (int j = 0; j < COLS; ++j) {
+      const int i = lane + 32 * j;
+      if (i < dim) {
+        const float xv = ld(xr + i), gv = ld(gr + i);
+        stg<T>(dx + row * dxs + i, r * gv * ld(w + i) - xv * c);
+        acc[j] = fmaf(gv, xv * r, acc[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < COLS; ++j) {
+    const int i = lane + 32 * j;
+    if (i < dim) atomicAdd(&dws[i], acc[j]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) atomicAdd(dw + i, dws[i]);
+}
+
+template <typename T, typename W>
+static int run_norm_bwd(const void* x, int64_t xs, const void* w, const float* rstd, const void* dy, int64_t dys,
+                        void* dx, int64_t dxs, float* dw, int64_t rows, int dim, cudaStream_t s) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t need = (rows + kNormThreads / 32 - 1) / (kNormThreads / 32);
+  const int grid = (int)(need < 4 * sms ? need : 4 * sms);
+  const int g = grid > 0 ? grid : 1;
+  if (dim <= 128)
+    rms_norm_bwd_kernel<T, W, 4><<<g, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, rstd, (const T*)dy, dys,
+                                                            (T*)dx, dxs, dw, rows, dim);
+  else if (dim <= 512)
+    rms_norm_bwd_kernel<T, W, 16><<<g, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, rstd, (const T*)dy, dys,
+                                                             (T*)dx, dxs, dw, rows, dim);
+  else
+    rms_norm_bwd_kernel<T, W, 64><<<g, kNormThreads, 0, s>>>((const T*)x, xs, (const W*)w, rstd, (const T*)dy, dys,
+                                                             (T*)dx, dxs, dw, rows, dim);
+  return check_launch("m3_rms_norm_bwd");
+}
+
+int launch_rms_norm_bwd(const void* x, int64_t xs, const void* w, const float* rstd, const void* dy, int64_t dys,
+                        void* dx, int64_t dxs, float* dw, int64_t rows, int dim, int x_dtype, int w_dtype,
+                        cudaStream_t s) {
+  const bool xb = x_dtype == M3_DTYPE_BF16, wb = w_dtype == M3_DTYPE_BF16;
+  if (xb) return wb ? run_norm_bwd<__nv_bfloat16, __nv_bfloat16>(x, xs, w, rstd, dy, dys, dx, dxs, dw, rows, dim, s)
+                    : run_norm_bwd<__nv_bfloat16, float>(x, xs, w, rstd, dy, dys, dx, dxs, dw, rows, dim, s);
+  return wb ? run_norm_bwd<float, __nv_bfloat16>(x, xs, w, rstd, dy, dys, dx, dxs, dw, rows, dim, s)
+            : run_norm_bwd<float, float>(x, xs, w, rstd, dy, dys, dx, dxs, dw, rows, dim, s);
 }
 
 }  // namespace m3

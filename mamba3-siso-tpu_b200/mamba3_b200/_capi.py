@@ -100,7 +100,7 @@ class M3DecodeArgs(ctypes.Structure):
 
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
-           "m3_device_error", "m3_copy2d_async", "m3_rms_norm")
+           "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd")
 
 _lib = None
 
@@ -131,8 +131,11 @@ def lib():
         L.m3_copy2d_async.argtypes = [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]
         L.m3_copy2d_async.restype = ctypes.c_int
         L.m3_rms_norm.argtypes = [_vp, ctypes.c_int64, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
-                                  ctypes.c_float, ctypes.c_int32, ctypes.c_int32, _vp]
+                                  ctypes.c_float, ctypes.c_int32, ctypes.c_int32, _vp, _vp]
         L.m3_rms_norm.restype = ctypes.c_int
+        L.m3_rms_norm_bwd.argtypes = [_vp, ctypes.c_int64, _vp, _vp, _vp, ctypes.c_int64, _vp, ctypes.c_int64, _vp,
+                                      ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp]
+        L.m3_rms_norm_bwd.restype = ctypes.c_int
         _lib = L
     return _lib
 

@@ -132,39 +132,82 @@ def split_in_proj(proj: torch.Tensor, cfg: SISOConfig):
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """``layer.py:190-198``: f32 internally, gain after scaling, cast back.
 
-    Without autograd (decode, inference) one fused kernel (`m3_rms_norm`) does it; with
-    autograd the torch ops below do, so that their backward exists."""
-    if _fused_norm_ok(x, weight):
-        return _rms_norm_fused(x, weight, eps)
+    On CUDA rows it is one fused kernel (`m3_rms_norm`), with a fused backward
+    (`m3_rms_norm_bwd`) when autograd needs one; other inputs take the torch ops below."""
+    rs = _row_stride(x, weight)
+    if rs is not None:
+        if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad):
+            if x.shape[-1] <= 2048:
+                return _RMSNormFn.apply(x, weight, eps)
+        else:
+            return _rms_norm_fused(x, weight, eps, rs)[0]
     xf = x.float()
     rstd = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return (xf * rstd * weight.float()).to(x.dtype)
 
 
-def _fused_norm_ok(x, weight) -> bool:
+def _row_stride(x, weight):
+    """The row stride of x viewed as (rows, dim), or None if the fused kernels do not apply."""
     if not (x.is_cuda and weight.is_cuda) or x.dim() < 1 or x.stride(-1) != 1 or weight.dim() != 1:
-        return False
+        return None
     if x.dtype not in (torch.bfloat16, torch.float32) or weight.dtype not in (torch.bfloat16, torch.float32):
-        return False
-    if torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad):
-        return False
-    if x.dim() > 2 and not x.is_contiguous():
-        return False
-    return weight.is_contiguous() and weight.shape[0] == x.shape[-1]
+        return None
+    if not weight.is_contiguous() or weight.shape[0] != x.shape[-1] or x.numel() == 0:
+        return None
+    if x.dim() == 1:
+        return x.shape[-1]
+    for d in range(x.dim() - 2):  # leading dims must collapse into one row index
+        if x.stride(d) != x.shape[d + 1] * x.stride(d + 1):
+            return None
+    return x.stride(-2)
 
 
-def _rms_norm_fused(x, weight, eps):
+def _fused_norm_ok(x, weight) -> bool:
+    return _row_stride(x, weight) is not None and not (torch.is_grad_enabled() and (x.requires_grad or
+                                                                                   weight.requires_grad))
+
+
+def _dtcode(t):
+    from . import _capi as C
+
+    return C.M3_DTYPE_BF16 if t.dtype == torch.bfloat16 else C.M3_DTYPE_F32
+
+
+def _rms_norm_fused(x, weight, eps, rs, want_rstd=False):
     from . import _capi as C
     from . import _tensors as T
 
     dim = x.shape[-1]
-    rows = x.numel() // dim if dim else 0
-    x_stride = x.stride(0) if x.dim() == 2 else dim
+    rows = x.numel() // dim
     y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
-    code = lambda t: C.M3_DTYPE_BF16 if t.dtype == torch.bfloat16 else C.M3_DTYPE_F32
-    C.check(C.lib().m3_rms_norm(T.ptr(x), x_stride, T.ptr(weight), T.ptr(y), dim, rows, dim, float(eps), code(x),
-                                code(weight), T.stream_handle(x.device)))
-    return y
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device) if want_rstd else None
+    C.check(C.lib().m3_rms_norm(T.ptr(x), rs, T.ptr(weight), T.ptr(y), dim, rows, dim, float(eps), _dtcode(x),
+                                _dtcode(weight), T.ptr(rstd), T.stream_handle(x.device)))
+    return y, rstd
+
+
+class _RMSNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        y, rstd = _rms_norm_fused(x, weight, eps, _row_stride(x, weight), want_rstd=True)
+        ctx.save_for_backward(x, weight, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from . import _capi as C
+        from . import _tensors as T
+
+        x, weight, rstd = ctx.saved_tensors
+        dim = x.shape[-1]
+        rows = x.numel() // dim
+        dy = dy.contiguous()
+        dx = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        dw = torch.zeros(dim, dtype=torch.float32, device=x.device)
+        C.check(C.lib().m3_rms_norm_bwd(T.ptr(x), _row_stride(x, weight), T.ptr(weight), T.ptr(rstd), T.ptr(dy), dim,
+                                        T.ptr(dx), dim, T.ptr(dw), rows, dim, _dtcode(x), _dtcode(weight),
+                                        T.stream_handle(x.device)))
+        return dx, dw.to(weight.dtype), None
 
 
 def _scalar_streams(proj: torch.Tensor, cfg: SISOConfig):

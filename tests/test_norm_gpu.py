@@ -43,3 +43,30 @@ def test_strided_rows_and_autograd_path():
     assert not LY._fused_norm_ok(xg, torch.ones(64, device="cuda"))
     LY.rms_norm(xg, torch.ones(64, device="cuda"), 1e-5).sum().backward()
     assert xg.grad is not None
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dim", [128, 512, 2048])
+def test_fused_backward_matches_autograd(dtype, dim):
+    """The fused autograd path (m3_rms_norm + m3_rms_norm_bwd) against torch autograd of the
+    formula, on a strided 3-D view of a wider row (the B / C slices of the in_proj output)."""
+    from mamba3_b200 import layer as LY
+
+    g = torch.Generator(device="cuda").manual_seed(9)
+    base = torch.randn(3, 50, dim + 64, device="cuda", generator=g).to(dtype)
+    w0 = (1 + 0.1 * torch.randn(dim, device="cuda", generator=g))
+    dy = torch.randn(3, 50, dim, device="cuda", generator=g).to(dtype)
+
+    xa = base.clone().requires_grad_(True)
+    wa = w0.clone().requires_grad_(True)
+    ya = LY.rms_norm(xa[..., 32:32 + dim], wa, 1e-5)
+    ya.backward(dy)
+    xb = base.clone().requires_grad_(True)
+    wb = w0.clone().requires_grad_(True)
+    yb = _ref(xb[..., 32:32 + dim], wb, 1e-5)
+    yb.backward(dy)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    rel = lambda a, b: float((a.detach().float() - b.detach().float()).norm() / b.detach().float().norm())
+    assert rel(ya, yb) < tol
+    assert rel(xa.grad, xb.grad) < tol
+    assert rel(wa.grad, wb.grad) < (1e-4 if dtype == torch.float32 else 2e-2)
