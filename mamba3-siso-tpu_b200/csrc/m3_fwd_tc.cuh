@@ -415,6 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
           for (int r = 0; r < 8; ++r) carry8[r] = wrap_fast(off[r]);
       }
       M3_TC_MARK(1);
+      umma::fence_async_smem();  // the q~ / khat tiles, for the MMAs issued below
+      umma::fence_before_sync();
       slot_sync(slot);
       float dg = 0.f;
       if constexpr (!STATES) {
@@ -426,6 +428,21 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       }
       slot_sync(slot);
 
+      // S = q~ khat^T and Yi = q~ S^T need nothing of phase 3: they run while it does
+      if constexpr (!STATES) {
+        umma::fence_after_sync();
+        if (ltid == 0) {
+          constexpr uint32_t id_s = umma::idesc_bf16(128, 128, false, false);
+          constexpr uint32_t id_yi = umma::idesc_bf16(128, 64, false, true);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
+            const uint64_t dq = umma::smem_desc(sQ + kmaj, 16, 1024);
+            umma::mma_bf16(tm + 0, dq, umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
+            umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + ks * 2048u, 16384, 1024), id_yi, ks > 0);
+          }
+        }
+      }
       M3_TC_MARK(2);
       // ---- phase 3: v and v exp2(A_last - A) tiles (MN-major: row = token) -------------
       uint32_t vreg[16];  // this thread's 32 v values (bf16 pairs), kept for the diagonal term
@@ -477,24 +494,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       umma::fence_after_sync();
 
       M3_TC_MARK(3);
-      // ---- phase 4: S, Yi, dSt on the tensor core ----------------------------------------
+      // ---- phase 4: the state update on the tensor core (S and Yi are already running) -----
       if (ltid == 0) {
-        constexpr uint32_t id_s = umma::idesc_bf16(128, 128, false, false);
-        constexpr uint32_t id_yi = umma::idesc_bf16(128, 64, false, true);
         constexpr uint32_t id_ds = umma::idesc_bf16(128, 64, true, true);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
           const uint32_t mn = ks * 2048u;
-          if constexpr (!STATES) {
-            const uint64_t dq = umma::smem_desc(sQ + kmaj, 16, 1024);
-            umma::mma_bf16(tm + 0, dq, umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
-            umma::mma_bf16(tm + 128, dq, umma::smem_desc(sSt + mn, 16384, 1024), id_yi, ks > 0);
-          }
           umma::mma_bf16(tm + 192, umma::smem_desc(sK + mn, 16384, 1024), umma::smem_desc(sVd + mn, 16384, 1024),
                          id_ds, true);
         }
-        umma::commit(&ss->mbar[0]);
+        umma::commit(&ss->mbar[0]);  // tracks S and Yi too (issued earlier by this thread)
       }
       if (slot_any(slot, !umma::mbar_wait(&ss->mbar[0], c & 1))) {
         if (ltid == 0) atomicExch(&g_m3_device_error, 1);
