@@ -59,3 +59,21 @@ def test_tc_backward_vs_exact_and_generic(shape, seeded):
     assert not bad, f"normwise errors vs exact above {BF16_GRAD_TOL}: {bad} (all {errs}; vs generic {vs_gen})"
     bad = {k: e for k, e in vs_gen.items() if not e < BF16_GRAD_TOL}
     assert not bad, f"normwise differences vs the generic kernel: {bad}"
+
+
+def test_tc_backward_without_gate_or_skip():
+    """No z (no gate, so no dz) and no D: the tensor-core backward against the generic one."""
+    from mamba3_b200 import kernel_bwd as KB
+    from tests.gpu_common import dev
+    from tests.test_bwd_gpu import _normwise
+
+    x, _, _ = _raw_case((1, 2, 256, 128, 64, 32, 128), False, seed=41)
+    io = lambda t: dev(t, torch.bfloat16)
+    args = (io(x["dy"]), io(x["q"]), io(x["k"]), io(x["v"]), dev(x["dt_raw"]), dev(x["a_raw"]), dev(x["trap_raw"]),
+            dev(x["angles"]), dev(x["dt_bias"]), dev(x["q_bias"]), dev(x["k_bias"]))
+    gt = KB.siso_backward_raw(*args, d_skip=None, z=None, chunk=128, dtype_policy="bf16", kernel="tensorcore")
+    gg = KB.siso_backward_raw(*args, d_skip=None, z=None, chunk=128, dtype_policy="bf16", kernel="generic")
+    assert gt.dz is None and gg.dz is None
+    for name in ("dq", "dk", "dv", "ddt_raw", "da_raw", "dtrap_raw", "dangles", "dq_bias", "dk_bias", "ddt_bias"):
+        e = _normwise(getattr(gt, name), getattr(gg, name))
+        assert e < 2e-2, f"{name}: {e}"
