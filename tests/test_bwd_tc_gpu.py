@@ -77,3 +77,33 @@ def test_tc_backward_without_gate_or_skip():
     for name in ("dq", "dk", "dv", "ddt_raw", "da_raw", "dtrap_raw", "dangles", "dq_bias", "dk_bias", "ddt_bias"):
         e = _normwise(getattr(gt, name), getattr(gg, name))
         assert e < 2e-2, f"{name}: {e}"
+
+
+@pytest.mark.parametrize("nr", [8])
+def test_tc_forward_backward_few_rotary_pairs(nr):
+    """n_angles = 8 (one rotary group; the other seven pass through): tensor-core forward and
+    backward against the generic kernels.  (n_angles = 0 is refused at the boundary, as the
+    reference's layer refuses a rotary fraction that leaves no angles.)"""
+    from mamba3_b200 import kernel_bwd as KB
+    from mamba3_b200 import kernel_fwd as KF
+    from tests.gpu_common import dev
+    from tests.metrics import rel_error
+    from tests.test_bwd_gpu import _normwise
+
+    x, _, _ = _raw_case((1, 2, 256, 128, 64, nr, 128), False, seed=43)
+    io = lambda t: dev(t, torch.bfloat16)
+    raw = (dev(x["dt_raw"]), dev(x["a_raw"]), dev(x["trap_raw"]), dev(x["angles"]), dev(x["dt_bias"]),
+           dev(x["q_bias"]), dev(x["k_bias"]))
+    yt = KF.siso_forward_raw(io(x["q"]), io(x["k"]), io(x["v"]), *raw, dev(x["d_skip"]), io(x["z"]), chunk=128,
+                             dtype_policy="bf16", kernel="tensorcore")[0]
+    yg = KF.siso_forward_raw(io(x["q"]), io(x["k"]), io(x["v"]), *raw, dev(x["d_skip"]), io(x["z"]), chunk=128,
+                             dtype_policy="bf16", kernel="generic")[0]
+    assert rel_error(yt, yg) < 2e-2
+    args = (io(x["dy"]), io(x["q"]), io(x["k"]), io(x["v"]), *raw)
+    gt = KB.siso_backward_raw(*args, d_skip=dev(x["d_skip"]), z=io(x["z"]), chunk=128, dtype_policy="bf16",
+                              kernel="tensorcore")
+    gg = KB.siso_backward_raw(*args, d_skip=dev(x["d_skip"]), z=io(x["z"]), chunk=128, dtype_policy="bf16",
+                              kernel="generic")
+    for name in ("dq", "dk", "dv", "dz", "ddt_raw", "da_raw", "dtrap_raw", "dq_bias", "dk_bias", "dangles"):
+        e = _normwise(getattr(gt, name), getattr(gg, name))
+        assert e < 2e-2, f"{name}: {e}"
