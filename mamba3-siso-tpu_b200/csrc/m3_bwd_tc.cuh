@@ -96,6 +96,10 @@ __device__ __forceinline__ float warp_suffix_scan(float x) {
   return x;
 }
 
+// RAW: the fused raw boundary (dt / A / trap streams and angles in, their gradients out);
+// otherwise the reference's preprocessed boundary (adt, gamma, scale, phi in; dadt,
+// dgamma, dscale, dphi, dseed_coef out: kernel_bwd.py:534-669).
+template <bool RAW>
 __global__ void __launch_bounds__(kThreads, 1)
     bwd_tc_kernel(const M3BwdArgs a, const uint8_t* __restrict__ tiles, const float* __restrict__ phis,
                   float* __restrict__ scratch) {
@@ -115,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const __nv_bfloat16* z = (const __nv_bfloat16*)a.z;
   const __nv_bfloat16* dy = (const __nv_bfloat16*)a.dy;
   const float Dh = a.d_skip ? a.d_skip[h] : 0.f;
-  const float dtb = a.dt_bias[h];
+  const float dtb = RAW ? a.dt_bias[h] : 0.f;
   float* phs = scratch + (size_t)blockIdx.x * (kScratchBytes / sizeof(float));  // [64][128]: phi, then dphi
   float* ths = phs + 64 * kC;                                                     // [64][128]: tanh(angles)
   uint4* rqs = reinterpret_cast<uint4*>(ths + 64 * kC);                            // [16][128]: raw q
@@ -144,7 +148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     G[i] = a.dfinal_ssm ? a.dfinal_ssm[(bh * kP + 32 * half + i) * kN + t] : 0.f;
   float dcarry8[8];  // adjoint of this warp's rotary-angle carry
 #pragma unroll
-  for (int r = 0; r < 8; ++r) dcarry8[r] = (a.dfinal_phi && 8 * warp + r < Nr) ? a.dfinal_phi[bh * Nr + 8 * warp + r] : 0.f;
+  for (int r = 0; r < 8; ++r)
+    dcarry8[r] = (RAW && a.dfinal_phi && 8 * warp + r < Nr) ? a.dfinal_phi[bh * Nr + 8 * warp + r] : 0.f;
   {
     // A_last term of the last chunk: sum(G o S_final); S_final is tile `nchunk`
     const uint8_t* sf = tiles + (bh * (nchunk + 1) + nchunk) * 16384u;
@@ -200,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = tid; i < kC * n4; i += kThreads) {
       const int row = i / n4, c4 = i - row * n4;
       umma::cp_async16(aAng + row * 256 + 16 * (c4 ^ (row & 15)),
-                       a.angles + (size_t)b * a.ang_st.b + (size_t)(tb + row) * a.ang_st.l + 4 * c4);
+                       RAW ? a.angles + (size_t)b * a.ang_st.b + (size_t)(tb + row) * a.ang_st.l + 4 * c4
+                           : a.phi + (bh * L + tb + row) * Nr + 4 * c4);
     }
     umma::cp_async_commit();
   };
@@ -232,17 +238,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float alast = ss->alast;
     // ---- P0: per-token scalars, g and e^A g (this chunk's tiles were prefetched) ---------
     const size_t ro = (size_t)b * a.raw_st.b + (size_t)tg * a.raw_st.l + (size_t)h * a.raw_st.h;
-    const float dt = softplusf(a.dt_raw[ro] + dtb);
-    const float lam = sigmoidf_(a.trap_raw[ro]);
-    const float ar = a.a_raw[ro];
-    const float av = fminf(-heavy_tail(ar), -a.a_floor);
-    float dtn = __shfl_down_sync(0xffffffffu, dt, 1), lamn = __shfl_down_sync(0xffffffffu, lam, 1);
-    if (lane == 31) {
-      dtn = tg + 1 < L ? softplusf(a.dt_raw[ro + a.raw_st.l] + dtb) : 0.f;
-      lamn = tg + 1 < L ? sigmoidf_(a.trap_raw[ro + a.raw_st.l]) : 0.f;
+    float dt = 0.f, lam = 0.f, ar = 0.f, av = 0.f, dtn = 0.f, lamn = 0.f, gam, scl, adtv;
+    if constexpr (RAW) {
+      dt = softplusf(a.dt_raw[ro] + dtb);
+      lam = sigmoidf_(a.trap_raw[ro]);
+      ar = a.a_raw[ro];
+      av = fminf(-heavy_tail(ar), -a.a_floor);
+      dtn = __shfl_down_sync(0xffffffffu, dt, 1);
+      lamn = __shfl_down_sync(0xffffffffu, lam, 1);
+      if (lane == 31) {
+        dtn = tg + 1 < L ? softplusf(a.dt_raw[ro + a.raw_st.l] + dtb) : 0.f;
+        lamn = tg + 1 < L ? sigmoidf_(a.trap_raw[ro + a.raw_st.l]) : 0.f;
+      }
+      gam = dt * lam;
+      scl = gam + dtn * (1.f - lamn);
+      adtv = av * dt;
+    } else {  // preprocessed boundary: (B, H, L) streams
+      adtv = a.adt[bh * L + tg];
+      gam = a.gamma[bh * L + tg];
+      scl = a.scale[bh * L + tg];
     }
-    const float gam = dt * lam, scl = gam + dtn * (1.f - lamn);
-    const float incl = warp_inclusive_scan(av * dt * kLog2e);
+    const float incl = warp_inclusive_scan(adtv * kLog2e);
     if (half == 0 && lane == 31) ss->wtot[warp & 3] = incl;
     if (half == 0) {
       reinterpret_cast<float*>(sm + kScrDt)[t] = dt;
@@ -304,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* kbp = ss->bias + kN + 8 * g;
       float off[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) off[r] = grot ? phis[(bh * nchunk + c) * Nr + 8 * g + r] : 0.f;
+      for (int r = 0; r < 8; ++r) off[r] = (RAW && grot) ? phis[(bh * nchunk + c) * Nr + 8 * g + r] : 0.f;
 #pragma unroll 1
       for (int i = 0; i < 2; ++i) {
         const int tb = 64 * i + 2 * lane;
@@ -320,9 +336,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint8_t* ap = sm + kAng + row * 256;
             const float4 lo = *reinterpret_cast<const float4*>(ap + 16 * ((2 * g) ^ (row & 15)));
             const float4 hi = *reinterpret_cast<const float4*>(ap + 16 * ((2 * g + 1) ^ (row & 15)));
-            ph[j][0] = tanh_acc(lo.x); ph[j][1] = tanh_acc(lo.y); ph[j][2] = tanh_acc(lo.z); ph[j][3] = tanh_acc(lo.w);
-            ph[j][4] = tanh_acc(hi.x); ph[j][5] = tanh_acc(hi.y); ph[j][6] = tanh_acc(hi.z); ph[j][7] = tanh_acc(hi.w);
+            ph[j][0] = lo.x; ph[j][1] = lo.y; ph[j][2] = lo.z; ph[j][3] = lo.w;
+            ph[j][4] = hi.x; ph[j][5] = hi.y; ph[j][6] = hi.z; ph[j][7] = hi.w;
           }
+          if constexpr (RAW) {  // raw angles -> cumulative angles (the preprocessed boundary gives phi)
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int r = 0; r < 8; ++r) ph[j][r] = tanh_acc(ph[j][r]);
 #pragma unroll
           for (int r = 0; r < 8; ++r)
             *reinterpret_cast<float2*>(ths + (8 * g + r) * kC + tb) = f2(ph[0][r], ph[1][r]);
@@ -334,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ph[1][r] = off[r] + inc;
             ph[0][r] = ph[1][r] - x1;
             off[r] += __shfl_sync(0xffffffffu, inc, 31);
+          }
           }
 #pragma unroll
           for (int r = 0; r < 8; ++r)
@@ -730,7 +752,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         red_add4(dst + (size_t)tt * kN, v.x, v.y, v.z, v.w);
       }
     }
-    {
+    if constexpr (!RAW) {
+      // preprocessed boundary: dphi is the pullback's per-token angle adjoint; the chunk's
+      // (128, Nr) block of dphi is contiguous
+      float* dst = a.dphi + (bh * L + t0) * Nr;
+      for (int idx = tid; idx < kC * Nr; idx += kThreads) {
+        const int tt = idx / Nr, r = idx - tt * Nr;
+        dst[idx] = phs[r * kC + tt];
+      }
+    } else {
       const int g = warp;
       const bool grot = 8 * g < Nr;
       float* dthp = reinterpret_cast<float*>(sm + kScrTh);  // [8][128]
@@ -789,13 +819,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       float dadt = sfx + alast;
       for (int w = (warp & 3) + 1; w < 4; ++w) dadt += ss->wtot[w];
       const float dscp = __shfl_up_sync(0xffffffffu, dscl, 1);
+      if (!RAW && half == 0) {  // kernel_bwd.py:592-600: the preprocessed boundary's scalar gradients
+        if (a.d_skip) dD_acc += qkd;
+        a.dadt[bh * L + tg] = dadt;
+        a.dgamma[bh * L + tg] = qkd * uwt;
+        a.dscale[bh * L + tg] = dscl;
+      }
       float dth = 0.f;
-      {
+      if (RAW) {
         const float* dthp = reinterpret_cast<const float*>(sm + kScrTh);
 #pragma unroll
         for (int gg = 0; gg < 8; ++gg) dth += dthp[gg * 128 + t];
       }
-      if (half == 0) {
+      if (RAW && half == 0) {
         float prev = dscp;
         if (lane == 0) prev = t > 0 ? part[t - 1] + part[256 + t - 1] : 0.f;
         const float dgam = qkd * uwt;
@@ -862,8 +898,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- seeds (kernel_bwd.py:636-646), angle carry, per-head reductions ------------------
     if (a.seed_ssm) {
       const size_t o0 = (size_t)b * a.raw_st.b + (size_t)h * a.raw_st.h;
-      const float dt0 = softplusf(a.dt_raw[o0] + dtb), lam0 = sigmoidf_(a.trap_raw[o0]);
-      const float coef = dt0 * (1.f - lam0);
+      float dt0 = 0.f, lam0 = 0.f, coef;
+      if constexpr (RAW) {
+        dt0 = softplusf(a.dt_raw[o0] + dtb);
+        lam0 = sigmoidf_(a.trap_raw[o0]);
+        coef = dt0 * (1.f - lam0);
+      } else {
+        coef = a.seed_coef[bh];
+      }
       const float kp = a.seed_k[bh * kN + t];
       float pk = 0.f, pc = 0.f;
 #pragma unroll
@@ -877,7 +919,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       atomicAdd(a.dseed_k + bh * kN + t, coef * pk);
       const float dcoef = cta_sum(pc, ss);
-      if (tid == 0) {
+      if (!RAW && tid == 0) a.dseed_coef[bh] = dcoef;
+      if (RAW && tid == 0) {
         const size_t od = (size_t)b * L * H + h;
         const float sg = sigmoidf_(a.dt_raw[o0] + dtb);
         const float e_dt = dcoef * (1.f - lam0) * sg;
@@ -886,7 +929,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         a.dtrap_raw[od] += -dcoef * dt0 * lam0 * (1.f - lam0);
       }
     }
-    if (a.dseed_phi && lane == 0 && 8 * warp < Nr)
+    if (RAW && a.dseed_phi && lane == 0 && 8 * warp < Nr)
 #pragma unroll
       for (int r = 0; r < 8; ++r) a.dseed_phi[bh * Nr + 8 * warp + r] = dcarry8[r];
     {
@@ -900,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float ddb = cta_sum(ddtb_acc, ss);
     if (tid == 0) {
       if (a.d_skip) atomicAdd(a.dd_skip + h, dD);
-      atomicAdd(a.ddt_bias + h, ddb);
+      if (RAW) atomicAdd(a.ddt_bias + h, ddb);
     }
   }
   umma::fence_before_sync();

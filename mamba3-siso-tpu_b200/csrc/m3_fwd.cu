@@ -99,12 +99,12 @@ size_t bwd_tc_workspace_bytes(const M3Dims& d) {
 }
 
 bool bwd_tc_eligible(const M3BwdArgs& a) {
-  if (!a.raw) return false;
   M3FwdArgs f{};
   f.dims = a.dims;
   f.io_dtype = a.io_dtype;
   f.policy = a.policy;
-  f.raw = 1;
+  f.raw = a.raw;
+  f.phi = a.phi;
   f.q = a.q; f.k = a.k; f.v = a.v; f.z = a.z;
   f.q_st = a.q_st; f.k_st = a.k_st; f.v_st = a.v_st; f.z_st = a.z_st;
   f.angles = a.angles; f.ang_st = a.ang_st;
@@ -129,30 +129,32 @@ int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s) {
   f.dims = d;
   f.io_dtype = a.io_dtype;
   f.policy = a.policy;
-  f.raw = 1;
+  f.raw = a.raw;
   f.a_floor = a.a_floor;
   f.q = a.q; f.k = a.k; f.v = a.v;
   f.q_st = a.q_st; f.k_st = a.k_st; f.v_st = a.v_st;
   f.dt_raw = a.dt_raw; f.a_raw = a.a_raw; f.trap_raw = a.trap_raw; f.raw_st = a.raw_st;
   f.angles = a.angles; f.ang_st = a.ang_st; f.dt_bias = a.dt_bias;
+  f.adt = a.adt; f.gamma = a.gamma; f.scale = a.scale; f.phi = a.phi;
   f.q_bias = a.q_bias; f.k_bias = a.k_bias; f.d_skip = a.d_skip;
   f.seed_ssm = a.seed_ssm; f.seed_k = a.seed_k; f.seed_v = a.seed_v; f.seed_phi = a.seed_phi;
+  f.seed_coef = a.seed_coef;
   int rc = launch_fwd_states_tc(f, tiles, phis, s);
   if (rc != M3_OK) return rc;
   if (a.seed_ssm) {
     cudaMemsetAsync(a.dseed_k, 0, (size_t)d.batch * d.nheads * d.state_dim * sizeof(float), s);
     cudaMemsetAsync(a.dseed_v, 0, (size_t)d.batch * d.nheads * d.headdim * sizeof(float), s);
   }
-  static bool attr_done[64] = {};
+  auto* kern = a.raw ? tcb::bwd_tc_kernel<true> : tcb::bwd_tc_kernel<false>;
+  static bool attr_done[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tcb::bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcb::kSmemBytes) !=
-        cudaSuccess)
+  if (dev < 64 && !attr_done[a.raw ? 1 : 0][dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tcb::kSmemBytes) != cudaSuccess)
       return check_launch("bwd_tc: cudaFuncSetAttribute");
-    attr_done[dev] = true;
+    attr_done[a.raw ? 1 : 0][dev] = true;
   }
-  tcb::bwd_tc_kernel<<<d.batch * d.nheads, tcb::kThreads, tcb::kSmemBytes, s>>>(a, tiles, phis, scratch);
+  kern<<<d.batch * d.nheads, tcb::kThreads, tcb::kSmemBytes, s>>>(a, tiles, phis, scratch);
   return check_launch("m3_siso_bwd (tensor core)");
 }
 

@@ -82,7 +82,7 @@ def _common(a, q, k, v, z, dy, dt_io):
 def siso_backward(dy, q, k, v, adt, gamma, scale, phi, q_bias, k_bias, ybar=None, chunk_states=None,
                   d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_coef=None,
                   dfinal_ssm=None, dfinal_k=None, dfinal_v=None, chunk: int = 128,
-                  dtype_policy: str = "bf16", workspace=None) -> SISOGrads:
+                  dtype_policy: str = "bf16", workspace=None, kernel: str = "auto") -> SISOGrads:
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape
@@ -126,6 +126,7 @@ def siso_backward(dy, q, k, v, adt, gamma, scale, phi, q_bias, k_bias, ybar=None
     a.dseed_ssm, a.dseed_k, a.dseed_v, a.dseed_coef = T.ptr(dss), T.ptr(dsk_), T.ptr(dsv), T.ptr(dsc)
     ws, need = _workspace(a.dims, dev, workspace)
     a.workspace, a.workspace_bytes = T.ptr(ws), need
+    a.kernel = {"auto": C.M3_KERNEL_AUTO, "generic": C.M3_KERNEL_GENERIC, "tensorcore": C.M3_KERNEL_TENSORCORE}[kernel]
     C.check(C.lib().m3_siso_bwd(a, T.stream_handle(dev)))
     return SISOGrads(dq=dq, dk=dk, dv=dv, dadt=dadt, dgamma=dgamma, dscale=dscale, dphi=dphi,
                      dq_bias=dqb, dk_bias=dkb, dd_skip=ddsk, dz=dz, dseed_ssm=dss, dseed_k=dsk_,

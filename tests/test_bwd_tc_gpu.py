@@ -107,3 +107,64 @@ def test_tc_forward_backward_few_rotary_pairs(nr):
     for name in ("dq", "dk", "dv", "dz", "ddt_raw", "da_raw", "dtrap_raw", "dq_bias", "dk_bias", "dangles"):
         e = _normwise(getattr(gt, name), getattr(gg, name))
         assert e < 2e-2, f"{name}: {e}"
+
+
+@pytest.mark.parametrize("seeded", [False, True])
+def test_tc_backward_preprocessed_boundary(seeded):
+    """The reference kernel's own boundary (adt, gamma, scale, phi in; their gradients and
+    dseed_coef out: ``kernel_bwd.py:534-669``) on the tensor-core backward, against exact
+    float64 gradients of the bf16-valued inputs and against the generic kernel."""
+    from mamba3_b200 import kernel_bwd as KB
+    from oracle import siso_oracle as O
+    from tests.gpu_common import dev, pre_inputs, rand_state
+    from tests.test_bwd_gpu import _normwise
+
+    b, h, l, n, p, nr, chunk = 2, 3, 256, 128, 64, 32, 128
+    x, pre = pre_inputs(b, h, l, n, p, nr, seed=47)
+    g = torch.Generator().manual_seed(9)
+    st = rand_state(b, h, p, n, nr) if seeded else None
+    coef = torch.rand(b, h, generator=g, dtype=torch.float64) * 0.05 if seeded else None
+    dfs = torch.randn(b, h, p, n, generator=g, dtype=torch.float64) * 0.1
+    dfk = torch.randn(b, h, n, generator=g, dtype=torch.float64) * 0.1
+    dfv = torch.randn(b, h, p, generator=g, dtype=torch.float64) * 0.1
+    r = lambda t: t.to(torch.bfloat16).double()
+    names = ["q", "k", "v", "adt", "gamma", "scale", "phi", "q_bias", "k_bias", "d_skip", "z"]
+    vals = dict(q=r(x["q"]), k=r(x["k"]), v=r(x["v"]), adt=pre.adt, gamma=pre.gamma, scale=pre.scale, phi=pre.phi,
+                q_bias=x["q_bias"], k_bias=x["k_bias"], d_skip=x["d_skip"], z=r(x["z"]))
+    dy = r(x["dy"])
+    leaves = {k_: v_.clone().requires_grad_(True) for k_, v_ in vals.items()}
+    if seeded:
+        cl = coef.clone().requires_grad_(True)
+        y, fin = O.siso_chunked(*(leaves[k_] for k_ in names), state=O.SISOState(st.ssm, st.k, st.v, st.phi),
+                                seed_dt=cl, seed_lam=torch.zeros_like(coef), chunk=chunk)
+    else:
+        y, fin = O.siso_chunked(*(leaves[k_] for k_ in names), chunk=chunk)
+    ((y * dy).sum() + (fin.ssm * dfs).sum() + (fin.k * dfk).sum() + (fin.v * dfv).sum()).backward()
+
+    io = lambda t: dev(t, torch.bfloat16)
+
+    def run(kernel):
+        return KB.siso_backward(io(dy), io(vals["q"]), io(vals["k"]), io(vals["v"]), dev(pre.adt), dev(pre.gamma),
+                                dev(pre.scale), dev(pre.phi), dev(x["q_bias"]), dev(x["k_bias"]),
+                                d_skip=dev(x["d_skip"]), z=io(vals["z"]),
+                                seed_ssm=dev(st.ssm) if seeded else None, seed_k=dev(st.k) if seeded else None,
+                                seed_v=dev(st.v) if seeded else None, seed_coef=dev(coef) if seeded else None,
+                                dfinal_ssm=dev(dfs), dfinal_k=dev(dfk), dfinal_v=dev(dfv), chunk=chunk,
+                                dtype_policy="bf16", kernel=kernel)
+
+    gt, gg = run("tensorcore"), run("generic")
+    pick = lambda gk: dict(q=gk.dq, k=gk.dk, v=gk.dv, adt=gk.dadt, gamma=gk.dgamma, scale=gk.dscale, phi=gk.dphi,
+                           q_bias=gk.dq_bias, k_bias=gk.dk_bias, d_skip=gk.dd_skip, z=gk.dz)
+    pt, pg = pick(gt), pick(gg)
+    errs = {k_: _normwise(pt[k_], leaves[k_].grad) for k_ in names}
+    vs_gen = {k_: _normwise(pt[k_], pg[k_]) for k_ in names}
+    if seeded:
+        errs["seed_coef"] = _normwise(gt.dseed_coef, cl.grad)
+        vs_gen["seed_coef"] = _normwise(gt.dseed_coef, gg.dseed_coef)
+        vs_gen["seed_ssm"] = _normwise(gt.dseed_ssm, gg.dseed_ssm)
+        vs_gen["seed_k"] = _normwise(gt.dseed_k, gg.dseed_k)
+        vs_gen["seed_v"] = _normwise(gt.dseed_v, gg.dseed_v)
+    bad = {k_: e for k_, e in errs.items() if not e < BF16_GRAD_TOL}
+    assert not bad, f"normwise errors vs exact above {BF16_GRAD_TOL}: {bad} (all {errs}; vs generic {vs_gen})"
+    bad = {k_: e for k_, e in vs_gen.items() if not e < BF16_GRAD_TOL}
+    assert not bad, f"normwise differences vs the generic kernel: {bad}"
