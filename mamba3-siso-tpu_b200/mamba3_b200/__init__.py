@@ -10,7 +10,7 @@ Module map (reference module -> this package):
 Every compute call goes through libm3siso.so (``_lib/``); there is no CPU path.
 """
 
-from . import layout, state  # noqa: F401
+from . import checkpoint, convert, layout, state  # noqa: F401
 from .layer import SISOConfig, SISOParams, init_params, mamba3_siso_layer, rms_norm, split_in_proj  # noqa: F401
 from .model import LMConfig, init_lm, lm_decode_step, lm_forward, zero_states  # noqa: F401
 from .siso import SISOOutput, siso_segment, siso_segment_streamed  # noqa: F401
