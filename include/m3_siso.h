@@ -224,6 +224,45 @@ int m3_rms_norm_bwd(const void *x, int64_t x_row_stride, const void *weight, con
                     int64_t dy_row_stride, void *dx, int64_t dx_row_stride, float *dweight, int64_t rows, int32_t dim,
                     int32_t x_dtype, int32_t w_dtype, void *stream);
 
+/* ---------------------------------------------------------------------------------
+ * Token sampling for generation (mamba3_pallas/train.py:454-500 `_pick_token`, and the
+ * window bookkeeping of train.py:559-579): per row, logits -> repetition penalty on the
+ * ids whose `seen_count` is > 0 (l / rep_penalty if l > 0 else l * rep_penalty), divide by
+ * temperature, keep the nucleus (descending order, ties by higher index first; an entry
+ * stays iff the mass strictly before it is < top_p), draw one id.  The draw is a
+ * function of (seed, row, counter[row]) only, so a replayed CUDA graph advances by the
+ * device-side counter.  After the draw: out_token[row] = id; history[row][counter] = id
+ * (if history and counter < history_cap); a stop id sets done[row] (rows with done set
+ * are skipped); otherwise the id enters the window ring (length rep_window, state
+ * [length, head] in window_state) and seen_count follows it.  counter[row] += 1.
+ * ------------------------------------------------------------------------------- */
+typedef struct M3SampleArgs {
+  int32_t batch, vocab;
+  int32_t logits_dtype;        /* M3_DTYPE_F32 or M3_DTYPE_BF16 */
+  int64_t logits_ld;           /* elements between rows (>= vocab) */
+  const void *logits;          /* (batch, logits_ld) */
+  float temperature, top_p, rep_penalty;
+  uint64_t seed;
+  int64_t *counter;            /* (batch,) draws so far; NULL = always 0 */
+  int32_t *seen_count;         /* (batch, vocab) window occurrence counts; NULL = no penalty */
+  int32_t *window;             /* (batch, rep_window) ring; NULL = no window update */
+  int32_t *window_state;       /* (batch, 2) [length, head] */
+  int32_t rep_window;
+  const int64_t *stop_ids;     /* n_stop ids (device) */
+  int32_t n_stop;
+  int32_t *done;               /* (batch,) or NULL */
+  int64_t *out_token;          /* (batch,) */
+  int64_t *history;            /* (batch, history_cap) or NULL */
+  int64_t history_cap;
+  void *scratch;               /* (batch, vocab) x 8 bytes of workspace; only read when
+                                  vocab > 184320 (else a row lives in shared memory), may
+                                  be NULL below that */
+  float *probs_out;            /* optional (batch, probs_ld): the filtered distribution */
+  int64_t probs_ld;
+} M3SampleArgs;
+
+int m3_sample_tokens(const M3SampleArgs *args, void *stream);
+
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);
 

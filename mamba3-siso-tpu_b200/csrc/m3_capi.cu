@@ -131,6 +131,26 @@ int m3_copy2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, si
   return M3_OK;
 }
 
+int m3_sample_tokens(const M3SampleArgs* args, void* stream) {
+  if (!args) return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: args is NULL");
+  const M3SampleArgs& a = *args;
+  if (!a.logits || !a.out_token || (a.vocab > 184320 && !a.scratch))
+    return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: NULL pointer");
+  if (a.batch < 0 || a.vocab <= 0 || a.vocab >= 8388608 || a.logits_ld < a.vocab || (a.probs_out && a.probs_ld < a.vocab))
+    return m3::set_error(M3_ERR_SHAPE, "m3_sample_tokens: bad batch / vocab / leading dimension");
+  if (a.logits_dtype != M3_DTYPE_F32 && a.logits_dtype != M3_DTYPE_BF16)
+    return m3::set_error(M3_ERR_UNSUPPORTED, "m3_sample_tokens: logits must be f32 or bf16");
+  if (!(a.temperature > 0.f) || !(a.rep_penalty > 0.f) || !(a.top_p >= 0.f))
+    return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: temperature and rep_penalty must be > 0, top_p >= 0");
+  if (a.window && (!a.window_state || !a.seen_count || a.rep_window <= 0))
+    return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: a window needs window_state, seen_count and rep_window > 0");
+  if (a.n_stop < 0 || (a.n_stop > 0 && !a.stop_ids)) return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: stop ids");
+  if (a.history && (!a.counter || a.history_cap <= 0))
+    return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: history needs a counter and history_cap > 0");
+  if (a.batch == 0) return M3_OK;
+  return m3::launch_sample(a, (cudaStream_t)stream);
+}
+
 int m3_device_error(int reset) {
   const int f = read_device_error(reset), d = read_decode_error(reset);
   return f != 0 ? f : d;

@@ -98,9 +98,19 @@ class M3DecodeArgs(ctypes.Structure):
     ]
 
 
+class M3SampleArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", _i32), ("vocab", _i32), ("logits_dtype", _i32), ("logits_ld", _i64), ("logits", _vp),
+        ("temperature", _f32), ("top_p", _f32), ("rep_penalty", _f32), ("seed", ctypes.c_uint64),
+        ("counter", _vp), ("seen_count", _vp), ("window", _vp), ("window_state", _vp), ("rep_window", _i32),
+        ("stop_ids", _vp), ("n_stop", _i32), ("done", _vp), ("out_token", _vp), ("history", _vp),
+        ("history_cap", _i64), ("scratch", _vp), ("probs_out", _vp), ("probs_ld", _i64),
+    ]
+
+
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
-           "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd")
+           "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens")
 
 _lib = None
 
@@ -128,6 +138,8 @@ def lib():
         L.m3_version.restype = ctypes.c_int
         L.m3_device_error.argtypes = [ctypes.c_int]
         L.m3_device_error.restype = ctypes.c_int
+        L.m3_sample_tokens.argtypes = [ctypes.POINTER(M3SampleArgs), _vp]
+        L.m3_sample_tokens.restype = ctypes.c_int
         L.m3_copy2d_async.argtypes = [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]
         L.m3_copy2d_async.restype = ctypes.c_int
         L.m3_rms_norm.argtypes = [_vp, ctypes.c_int64, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,

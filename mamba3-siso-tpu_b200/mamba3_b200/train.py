@@ -16,7 +16,10 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
+from . import _capi as C
+from . import _tensors as T
 from . import model as M
+from .sampling import TokenSampler
 
 
 def param_list(params: M.LMParams) -> List[torch.Tensor]:
@@ -123,70 +126,107 @@ def make_step(cfg: M.LMConfig, params: M.LMParams, lr: float = 1e-3, betas=(0.9,
     return step
 
 
-def _pick_token(logits: torch.Tensor, seen: torch.Tensor, gen: torch.Generator, temperature: float,
-                top_p: float, rep_penalty: float, vocab: int) -> torch.Tensor:
-    """``train.py:454-500``: sign-aware repetition penalty, temperature, nucleus filter
-    (the top-1 is always kept), then a categorical draw.  All on the device."""
-    lg = logits.float()
-    pen = torch.where(lg > 0, lg / rep_penalty, lg * rep_penalty)
-    lg = torch.where(seen, pen, lg) / temperature
-    srt, order = torch.sort(lg, descending=True)
-    probs = torch.softmax(srt, dim=-1)
-    keep = (torch.cumsum(probs, dim=-1) - probs) < top_p
-    masked = torch.where(keep, srt, torch.full_like(srt, float("-inf")))
-    lg = torch.full_like(lg, float("-inf")).scatter(-1, order, masked)
-    p = torch.softmax(lg, dim=-1)
-    return torch.multinomial(p, 1, generator=gen).squeeze(-1) % vocab
+def _seed_from(key, device) -> int:
+    """A 64-bit sampler seed from an int or a torch.Generator (one draw from it)."""
+    if isinstance(key, torch.Generator):
+        return int(torch.randint(0, 2**62, (1,), generator=key, device=key.device))
+    return int(key)
+
+
+def _pick_token(logits: torch.Tensor, seen: torch.Tensor, gen, temperature: float, top_p: float,
+                rep_penalty: float, vocab: int) -> torch.Tensor:
+    """``train.py:454-500``: repetition penalty on ``seen`` (bool ``(vocab,)``), temperature,
+    nucleus filter, one categorical draw -- the ``m3_sample_tokens`` kernel, one row."""
+    smp = TokenSampler(1, vocab, logits.device, seed=_seed_from(gen, logits.device), temperature=temperature,
+                       top_p=top_p, rep_penalty=rep_penalty)
+    smp.seen.copy_(seen.reshape(1, -1)[:, :vocab].to(torch.int32))
+    a = smp._args(logits.reshape(1, -1), update=False)
+    C.check(C.lib().m3_sample_tokens(a, T.stream_handle(logits.device)))
+    return smp.token[0].clone()
+
+
+class _GenerateGraph:
+    """One decode step fed by the sampler's token buffer, then the sampler writing the next
+    token into that buffer, captured once as a CUDA graph: each replay generates a token
+    with no host involvement.  The warm-up runs leave the per-layer states as they were."""
+
+    def __init__(self, params, cfg, states, smp: TokenSampler, compute_dtype):
+        dev = params.embed.device
+        snap = [[t.clone() for t in st] for st in states]
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for st, sn in zip(states, snap):
+            for t, s0 in zip(st, sn):
+                t.copy_(s0)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            logits, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+            smp.pick(logits)
+
+    def replay(self):
+        self.graph.replay()
 
 
 @torch.no_grad()
 def generate(params: M.LMParams, cfg: M.LMConfig, key, prompt_ids, n_tokens: int = 192, temperature: float = 0.9,
              top_p: float = 0.95, rep_penalty: float = 1.15, rep_window: int = 64,
              stop_ids: Optional[Iterable[int]] = None, on_token: Optional[Callable[[int], None]] = None,
-             compute_dtype=None) -> List[int]:
-    """``train.py:503-582``: prefill the prompt in whole chunks, feed the remainder
-    token by token through `model.lm_decode_step`, then sample ``n_tokens``."""
+             compute_dtype=None, device_loop: bool = True, sync_every: int = 32) -> List[int]:
+    """``train.py:503-582``: prefill the prompt in whole chunks, feed the remainder token
+    by token through `model.lm_decode_step`, then sample ``n_tokens`` (fewer if a stop id
+    is drawn; it is included, as in the reference).
+
+    Sampling, the repetition window and the stop test run on the device
+    (`sampling.TokenSampler`).  With ``device_loop`` the decode step and the sampler are
+    one CUDA graph replayed per token, and the host looks at the device only every
+    ``sync_every`` tokens (stop test, ``on_token`` delivery); otherwise the same kernels
+    are launched eagerly per token.  ``key`` (int or torch.Generator) seeds the draw; the
+    random stream differs from JAX's, so ids match the reference in distribution only."""
     ids = [int(t) for t in np.asarray(prompt_ids).reshape(-1)]
     if not ids:
         raise ValueError("prompt_ids is empty; at least one token is needed")
     dev = params.embed.device
     chunk = cfg.siso.chunk
-    gen = key if isinstance(key, torch.Generator) else torch.Generator(device=dev).manual_seed(int(key))
     states = M.zero_states(cfg, 1, device=dev)
     n_whole = (len(ids) - 1) // chunk * chunk
     last = None
     if n_whole:
         logits, states = M.lm_forward(params, torch.tensor([ids[:n_whole]], device=dev), cfg, states=states,
-                                      compute_dtype=compute_dtype)
-        last = logits[0, -1]
+                                      compute_dtype=compute_dtype, logits="last")
+        last = logits
     for t in ids[n_whole:]:
-        logits, states = M.lm_decode_step(params, torch.tensor([t], device=dev), states, cfg,
-                                          compute_dtype=compute_dtype)
-        last = logits[0]
-    seen = torch.zeros(cfg.vocab_size, dtype=torch.bool, device=dev)
-    window = ids[-rep_window:]
-    for t in window:
-        seen[t] = True
-    out = list(ids)
-    window = list(window)
-    stop = set(stop_ids) if stop_ids else set()
-    for _ in range(n_tokens):
-        nxt = int(_pick_token(last, seen, gen, temperature, top_p, rep_penalty, cfg.vocab_size))
-        out.append(nxt)
-        if on_token is not None:
-            on_token(nxt)
-        if nxt in stop:
+        last, states = M.lm_decode_step(params, torch.tensor([t], device=dev), states, cfg,
+                                        compute_dtype=compute_dtype)
+    if n_tokens <= 0:
+        return ids
+    smp = TokenSampler(1, cfg.vocab_size, dev, seed=_seed_from(key, dev), temperature=temperature, top_p=top_p,
+                       rep_penalty=rep_penalty, rep_window=rep_window, stop_ids=stop_ids, history_cap=n_tokens)
+    smp.reset([ids])
+    smp.pick(last.reshape(1, -1))
+    step = None
+    if device_loop and n_tokens > 1:
+        step = _GenerateGraph(params, cfg, states, smp, compute_dtype).replay
+    elif n_tokens > 1:
+        def step():
+            lg, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+            smp.pick(lg)
+    produced, delivered = 1, 0
+    while True:
+        n_drawn, done = (int(v) for v in torch.stack([smp.counter[0], smp.done[0].long()]).tolist())
+        if on_token is not None and n_drawn > delivered:
+            for t in smp.history[0, delivered:n_drawn].tolist():
+                on_token(int(t))
+            delivered = n_drawn
+        if done or produced >= n_tokens:
             break
-        window.append(nxt)
-        if len(window) > rep_window:
-            dropped = window.pop(0)
-            if dropped not in window:
-                seen[dropped] = False
-        seen[nxt] = True
-        logits, states = M.lm_decode_step(params, torch.tensor([nxt], device=dev), states, cfg,
-                                          compute_dtype=compute_dtype)
-        last = logits[0]
-    return out
+        for _ in range(min(max(1, sync_every), n_tokens - produced)):
+            step()
+            produced += 1
+    return ids + smp.history[0, :n_drawn].tolist()
 
 
 def sample(params: M.LMParams, cfg: M.LMConfig, key, prompt: bytes = b"the ", n_tokens: int = 192,

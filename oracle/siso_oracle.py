@@ -393,3 +393,28 @@ def layer_forward(params: dict, u, *, d_state, headdim, nheads, n_angles, chunk,
     bsz, seqlen = u.shape[:2]
     y = y.transpose(1, 2).reshape(bsz, seqlen, d_inner)
     return y @ params["out_proj"], st
+
+
+# --------------------------------------------------------------------------------------
+# sampling filter: train.py:454-500 (_pick_token, before the categorical draw)
+# --------------------------------------------------------------------------------------
+
+
+def nucleus_probs(logits, seen, temperature, top_p, rep_penalty):
+    """``train.py:483-498``: the distribution ``_pick_token`` draws from, per row.
+
+    Sign-aware repetition penalty on ``seen`` ids, division by the temperature, then the
+    nucleus: sort descending -- ``argsort(lg)[::-1]``, so among equal values the higher
+    index comes first -- and keep an entry iff the softmax mass strictly before it is
+    < top_p.  Returns the softmax over the kept entries (zeros elsewhere), in the dtype of
+    ``logits`` (float64 recommended).  ``logits`` ``(R, V)``, ``seen`` bool ``(R, V)``."""
+    lg = torch.where(seen, torch.where(logits > 0, logits / rep_penalty, logits * rep_penalty), logits)
+    lg = lg / temperature
+    # stable ascending sort, then reversed: ties end up in descending index order
+    order = torch.sort(lg, dim=-1, stable=True).indices.flip(-1)
+    srt = torch.gather(lg, -1, order)
+    probs = torch.softmax(srt, dim=-1)
+    keep = (torch.cumsum(probs, dim=-1) - probs) < top_p
+    masked = torch.where(keep, srt, torch.full_like(srt, -math.inf))
+    out = torch.full_like(lg, -math.inf).scatter(-1, order, masked)
+    return torch.softmax(out, dim=-1)

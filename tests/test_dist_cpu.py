@@ -35,7 +35,8 @@ def _worker(rank, world, port, q):
     loss = ((x @ ws[0] + ws[1]) @ ws[2]).pow(2).sum()
     loss.backward()
     bk.finish()
-    q.put((rank, [w.grad.clone() for w in ws]))
+    # numpy copies travel by value (a shared tensor's storage can vanish with the process)
+    q.put((rank, [w.grad.clone().numpy() for w in ws]))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -47,7 +48,7 @@ def test_bucketed_allreduce_mean_gloo():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=120) for _ in procs)
+    res = {r: [torch.from_numpy(a) for a in gs] for r, gs in (q.get(timeout=120) for _ in procs)}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
