@@ -40,6 +40,8 @@ int main(void) {
          sizeof(M3BwdArgs), sizeof(M3DecodeArgs));
   printf("%zu %zu %zu\n", offsetof(M3FwdArgs, chunk_states_dtype), offsetof(M3BwdArgs, workspace_bytes),
          offsetof(M3DecodeArgs, y));
+  printf("%zu %zu %zu %zu\n", sizeof(M3SampleArgs), offsetof(M3SampleArgs, seed), offsetof(M3SampleArgs, stop_ids),
+         offsetof(M3SampleArgs, probs_ld));
   return 0;
 }
 '''
@@ -52,7 +54,9 @@ int main(void) {
     got = [int(x) for x in out]
     want = [ctypes.sizeof(C.M3Dims), ctypes.sizeof(C.M3Strides), ctypes.sizeof(C.M3FwdArgs),
             ctypes.sizeof(C.M3BwdArgs), ctypes.sizeof(C.M3DecodeArgs),
-            C.M3FwdArgs.chunk_states_dtype.offset, C.M3BwdArgs.workspace_bytes.offset, C.M3DecodeArgs.y.offset]
+            C.M3FwdArgs.chunk_states_dtype.offset, C.M3BwdArgs.workspace_bytes.offset, C.M3DecodeArgs.y.offset,
+            ctypes.sizeof(C.M3SampleArgs), C.M3SampleArgs.seed.offset, C.M3SampleArgs.stop_ids.offset,
+            C.M3SampleArgs.probs_ld.offset]
     assert got == want
 
 
@@ -106,3 +110,22 @@ def test_decode_validation():
     assert C.lib().m3_siso_decode(a, None) == C.M3_ERR_UNSUPPORTED
     a.state_dim = 32
     assert C.lib().m3_siso_decode(a, None) == C.M3_ERR_ARG
+
+
+def test_sample_validation():
+    """Argument checks of m3_sample_tokens run on the host, before any launch."""
+    a = C.M3SampleArgs()
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_ARG  # no logits / output
+    a.logits, a.out_token = 16, 16  # never dereferenced: validation fails first
+    a.batch, a.vocab, a.logits_ld = 1, 100, 50
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_SHAPE  # leading dimension < vocab
+    a.logits_ld, a.logits_dtype = 100, 7
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_UNSUPPORTED
+    a.logits_dtype, a.temperature, a.rep_penalty, a.top_p = C.M3_DTYPE_F32, 0.0, 1.0, 0.9
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_ARG  # temperature must be > 0
+    a.temperature, a.window, a.rep_window = 1.0, 16, 0
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_ARG  # window without its state
+    a.window, a.history = None, 16
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_ARG  # history without a counter
+    a.history, a.batch = None, 0
+    assert C.lib().m3_sample_tokens(a, None) == C.M3_OK  # nothing to do
