@@ -13,7 +13,7 @@ Every compute call goes through libm3siso.so (``_lib/``); there is no CPU path.
 from . import checkpoint, convert, layout, state  # noqa: F401
 from .layer import SISOConfig, SISOParams, init_params, mamba3_siso_layer, rms_norm, split_in_proj  # noqa: F401
 from .model import LMConfig, init_lm, lm_decode_step, lm_forward, zero_states  # noqa: F401
-from .siso import SISOOutput, siso_segment, siso_segment_streamed  # noqa: F401
+from .siso import SISOOutput, siso_segment, siso_segment_seq_parallel, siso_segment_streamed  # noqa: F401
 from .state import SISOState, zero_state  # noqa: F401
 
 __version__ = "0.1.0"

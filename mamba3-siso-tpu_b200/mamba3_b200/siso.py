@@ -203,3 +203,93 @@ def siso_segment_streamed(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
         t.record_stream(s_in)
     cur.wait_stream(s_out)
     return SISOOutput(y=y_out, state=state)
+
+
+@torch.no_grad()
+def siso_segment_seq_parallel(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=None,
+                              z=None, state: Optional[SISOState] = None, a_floor: float = 1e-4, chunk: int = 128,
+                              policy_name: str = "bf16", group=None, segment_fn=None) -> SISOOutput:
+    """Sequence-parallel prefill: rank r of ``group`` holds the r-th contiguous L-slice of
+    the same sequences (every other argument as for `siso_segment`; ``state`` is the
+    carry entering rank 0's slice and is ignored on the other ranks).  Returns this
+    rank's y and the exact carry at the end of its slice -- on the last rank, the state
+    after the whole sequence.  Forward only.
+
+    The chained-segment result (``siso.py:154-216`` applied slice after slice) is
+    reached with two scans per rank and two all-gathers, no rank waiting on another's scan:
+
+    1. The cumulative angle entering slice r is the carry's phi plus the earlier slices'
+       sums of tanh(angle) pi dt (mod 2 pi), from an all-gather of each slice's sum.
+    2. Scan 1 runs the slice from (ssm 0, k 0, v 0, phi_in): its final ssm S_r holds
+       everything the slice itself adds, its final k and v are the true last-token ones.
+    3. A carry enters a slice as the seeded state S_in + coef v_prev k_prev^T (coef =
+       dt_1 (1 - lam_1) of the slice's first token, ``siso.py:207``), which the slice only
+       decays, by e^{A} with A the slice's sum of adt.  So after an all-gather of
+       (S_r, k_r, v_r, A_r, coef_r) every rank rebuilds
+       S_end(j) = e^{A_j} (S_end(j-1) + coef_j v_{j-1} k_{j-1}^T) + S_j for the slices
+       before it.
+    4. Scan 2 runs the slice from the true carry (S_end(r-1), k_{r-1}, v_{r-1}, phi_in).
+
+    ``segment_fn`` replaces `siso_segment` (same signature and result); tests use it to
+    run the exchange logic on CPU ranks.
+    """
+    import torch.distributed as dist
+
+    from .state import heavy_tail
+
+    seg = segment_fn or siso_segment
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    b, h, p, n, nr = v.shape[0], v.shape[1], v.shape[-1], q.shape[-1], angles.shape[-1]
+    dev, f32 = v.device, torch.float32
+    if state is None:
+        state = SISOState(ssm=torch.zeros(b, h, p, n, dtype=f32, device=dev),
+                          k=torch.zeros(b, h, n, dtype=f32, device=dev),
+                          v=torch.zeros(b, h, p, dtype=f32, device=dev),
+                          phi=torch.zeros(b, h, nr, dtype=f32, device=dev))
+
+    def gather(t):
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t.contiguous(), group=group)
+        return out
+
+    # per-slice scalars of the preprocessing (reference.py:160-199), float64 sums
+    dt = torch.nn.functional.softplus(dt_raw.double() + dt_bias.double())             # (B, L, H)
+    adt = torch.clamp(-heavy_tail(a_raw.double()), max=-a_floor) * dt
+    lam = torch.sigmoid(trap_raw.double())
+    inc = torch.einsum("blh,blr->bhr", dt, torch.tanh(angles.double())) * torch.pi  # angle increment
+    a_all = adt.sum(1)                                                               # (B, H)
+    coef = dt[:, 0] * (1.0 - lam[:, 0])
+    # 1. entering angles
+    incs = gather(inc)
+    phi_in = gather(state.phi.double())[0].clone()  # rank 0's carry
+    for j in range(rank):
+        phi_in = phi_in + incs[j]
+    phi_in = torch.remainder(phi_in, 2 * torch.pi).to(f32)
+    if rank != 0:
+        state = None  # only rank 0's carry is the caller's
+    # 2. scan 1 from a zero carry at the true entering angle
+    zero = SISOState(ssm=torch.zeros(b, h, p, n, dtype=f32, device=dev), k=torch.zeros(b, h, n, dtype=f32, device=dev),
+                     v=torch.zeros(b, h, p, dtype=f32, device=dev), phi=phi_in)
+    kw = dict(a_floor=a_floor, chunk=chunk, policy_name=policy_name)
+    first = seg(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z, state=zero, **kw)
+    # 3. exchange and rebuild the carry entering this slice
+    f0 = first.state
+    parts = gather(torch.cat([f0.ssm.reshape(b, h, -1).double(), f0.k.reshape(b, h, -1).double(),
+                              f0.v.reshape(b, h, -1).double(), a_all[..., None], coef[..., None]], dim=-1))
+    carry0 = gather(torch.cat([s.reshape(b, h, -1).double() for s in
+                               (state if state is not None else zero)[:3]], dim=-1))[0]
+    s_end = carry0[..., :p * n].reshape(b, h, p, n)
+    k_end = carry0[..., p * n:p * n + n]
+    v_end = carry0[..., p * n + n:p * n + n + p]
+    for j in range(rank):
+        pj = parts[j]
+        s_j = pj[..., :p * n].reshape(b, h, p, n)
+        k_j, v_j = pj[..., p * n:p * n + n], pj[..., p * n + n:p * n + n + p]
+        aj, cj = pj[..., -2], pj[..., -1]
+        s_end = torch.exp(aj)[..., None, None] * (s_end + cj[..., None, None] * v_end[..., :, None] * k_end[..., None, :])
+        s_end = s_end + s_j
+        k_end, v_end = k_j, v_j
+    carry = SISOState(ssm=s_end.to(f32), k=k_end.to(f32), v=v_end.to(f32), phi=phi_in)
+    # 4. scan 2 from the true carry
+    return seg(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z, state=carry, **kw)
