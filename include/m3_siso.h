@@ -194,6 +194,13 @@ typedef struct M3DecodeArgs {
   const float *q_bias, *k_bias, *d_skip;
   float *ssm, *state_k, *state_v, *phi;   /* in/out */
   void *y;                    /* (B, H, P) io_dtype */
+  /* Fusions for lm_decode_step (a zeroed tail keeps the plain behaviour): */
+  int32_t scalar_dtype;       /* M3_DTYPE_* of dt_raw / a_raw / trap_raw (or adt / dt / lam) and
+                                 angles: the in_proj columns can be read as they are */
+  const float *q_norm_w, *k_norm_w;  /* (N) gains: q and k are the raw C / B columns and are
+                                 RMS-normalised in the kernel (layer.py:190-198: fp32 math,
+                                 rounded to io_dtype) before the biases; NULL = already normed */
+  float norm_eps;
 } M3DecodeArgs;
 
 int m3_siso_decode(const M3DecodeArgs *args, void *stream);

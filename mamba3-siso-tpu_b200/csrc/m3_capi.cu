@@ -265,6 +265,10 @@ int m3_siso_decode(const M3DecodeArgs* args, void* stream) {
     return set_error(M3_ERR_ARG, "decode needs adt, dt, lam");
   }
   if (((uintptr_t)a.ssm) % 16 != 0) return set_error(M3_ERR_ARG, "ssm must be 16-byte aligned");
+  if (a.scalar_dtype != M3_DTYPE_F32 && a.scalar_dtype != M3_DTYPE_BF16)
+    return set_error(M3_ERR_UNSUPPORTED, "scalar_dtype must be f32 or bf16");
+  if ((a.q_norm_w == nullptr) != (a.k_norm_w == nullptr))
+    return set_error(M3_ERR_ARG, "q_norm_w and k_norm_w go together");
   if (a.qk_stride_b == 0) a.qk_stride_b = a.state_dim;
   if (a.vz_stride_b == 0) a.vz_stride_b = (int64_t)a.nheads * a.headdim;
   if (a.raw_stride_b == 0) a.raw_stride_b = a.nheads;

@@ -24,6 +24,12 @@
 
 namespace m3 {
 
+template <typename T> __device__ __forceinline__ float rnd_io(float x);
+template <> __device__ __forceinline__ float rnd_io<float>(float x) { return x; }
+template <> __device__ __forceinline__ float rnd_io<__nv_bfloat16>(float x) {
+  return __bfloat162float(__float2bfloat16(x));
+}
+
 constexpr int kDecThreads = 256;
 constexpr int kDecCtasPerSm = 3;
 
@@ -71,6 +77,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
   __shared__ __align__(16) float s_q[N], s_k[N], s_kp[N];  // q~ (readout-rounded), k~, previous k~
   __shared__ float s_bv[P], s_gv[P], s_dv[P], s_gate[P];  // beta v_prev, gamma v, D v, silu(z)
   __shared__ float s_ph[64];
+  __shared__ float s_ssq[2][4];  // per-warp sums of q^2, k^2 for the fused norms
   const int tid = threadIdx.x;
   const int H = a.nheads, Nr = a.n_angles;
   const int total = a.batch * H;
@@ -92,39 +99,44 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
   // latency overlaps the previous item's update.
   struct In {
     float dtr, ar, trr;       // raw dt / A / trap (or adt / dt / lam)
-    float u, w, um, wm, kpv;  // column threads: q + q_bias, k + k_bias, their pair partners, k_prev
+    float u, w, um, wm, kpv;  // column threads: q, k, their pair partners (biases not yet added), k_prev
     float ph, an;             // angle threads: phi, raw angle
     float vc, vp, zz;         // row threads: v, v_prev, z
   };
   const int n = tid, j = n < H2 ? n : n - H2;
+  const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
+  const bool sbf = a.scalar_dtype == M3_DTYPE_BF16;
+  auto lds = [&](const float* p, size_t i) {  // a scalar-stream element in scalar_dtype
+    return sbf ? ld(reinterpret_cast<const __nv_bfloat16*>(p) + i) : p[i];
+  };
+  const bool fnorm = a.q_norm_w != nullptr;
   auto load_in = [&](int item, In& x) {
     const int b = item / H, h = item % H;
     const size_t bh = (size_t)item;
     if (a.raw) {
       const size_t o = (size_t)b * a.raw_stride_b + h;
-      x.dtr = a.dt_raw[o] + a.dt_bias[h];
-      x.ar = a.a_raw[o];
-      x.trr = a.trap_raw[o];
+      x.dtr = lds(a.dt_raw, o) + a.dt_bias[h];
+      x.ar = lds(a.a_raw, o);
+      x.trr = lds(a.trap_raw, o);
     } else {
-      x.dtr = a.adt[bh];
-      x.ar = a.dt[bh];
-      x.trr = a.lam[bh];
+      x.dtr = lds(a.adt, bh);
+      x.ar = lds(a.dt, bh);
+      x.trr = lds(a.lam, bh);
     }
     if (tid < N) {
       const T* q = (const T*)a.q + (size_t)b * a.qk_stride_b;
       const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
-      const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
-      x.u = ld(q + n) + a.q_bias[h * N + n];
-      x.w = ld(k + n) + a.k_bias[h * N + n];
+      x.u = ld(q + n);
+      x.w = ld(k + n);
       if (j < Nr) {
-        x.um = ld(q + mm) + a.q_bias[h * N + mm];
-        x.wm = ld(k + mm) + a.k_bias[h * N + mm];
+        x.um = ld(q + mm);
+        x.wm = ld(k + mm);
       }
       x.kpv = a.state_k[bh * N + n];
     }
     if (tid < Nr) {
       x.ph = a.phi[bh * Nr + tid];
-      x.an = a.angles[(size_t)b * a.ang_stride_b + tid];
+      x.an = lds(a.angles, (size_t)b * a.ang_stride_b + tid);
     }
     if (tid >= 128 && tid < 128 + P) {
       const int p = tid - 128;
@@ -165,6 +177,17 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
     const float gamma = dt * lam;
 
     // ---- preamble: advanced angles, per-row coefficients --------------------------------------
+    if (fnorm && tid < 128) {  // per-warp sums of squares of the raw q / k row
+      float sq = tid < N ? cur.u * cur.u : 0.f, sk = tid < N ? cur.w * cur.w : 0.f;
+      for (int o = 16; o; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      }
+      if ((tid & 31) == 0) {
+        s_ssq[0][tid >> 5] = sq;
+        s_ssq[1][tid >> 5] = sk;
+      }
+    }
     if (tid < Nr) s_ph[tid] = wrap_fast(cur.ph + tanh_acc(cur.an) * kPi * dt);
     if (tid >= 128 && tid < 128 + P) {
       const int p = tid - 128;
@@ -177,13 +200,30 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
     __syncthreads();
     // rotary columns: x cos + rot_half(x) sin, rot_half = [-hi, lo]  (layout.py:375-398)
     if (tid < N) {
-      float qv = cur.u, kv = cur.w;
+      float u = cur.u, w = cur.w, um = cur.um, wm = cur.wm;
+      if (fnorm) {  // layer.py:190-198 on the C / B columns, rounded to the I/O dtype like the layer's norm
+        const float rq = rsqrtf((s_ssq[0][0] + s_ssq[0][1] + s_ssq[0][2] + s_ssq[0][3]) / N + a.norm_eps);
+        const float rk = rsqrtf((s_ssq[1][0] + s_ssq[1][1] + s_ssq[1][2] + s_ssq[1][3]) / N + a.norm_eps);
+        u = rnd_io<T>(u * rq * a.q_norm_w[n]);
+        w = rnd_io<T>(w * rk * a.k_norm_w[n]);
+        if (j < Nr) {
+          um = rnd_io<T>(um * rq * a.q_norm_w[mm]);
+          wm = rnd_io<T>(wm * rk * a.k_norm_w[mm]);
+        }
+      }
+      u += a.q_bias[h * N + n];
+      w += a.k_bias[h * N + n];
+      if (j < Nr) {
+        um += a.q_bias[h * N + mm];
+        wm += a.k_bias[h * N + mm];
+      }
+      float qv = u, kv = w;
       if (j < Nr) {
         float sn, cs;
         sincos_wrapped(s_ph[j], &sn, &cs);
         const float sgn = n < H2 ? -1.f : 1.f;
-        qv = cur.u * cs + sgn * cur.um * sn;
-        kv = cur.w * cs + sgn * cur.wm * sn;
+        qv = u * cs + sgn * um * sn;
+        kv = w * cs + sgn * wm * sn;
       }
       s_q[n] = mmr<MMB>(qv);
       s_k[n] = kv;

@@ -95,6 +95,7 @@ class M3DecodeArgs(ctypes.Structure):
         ("q_bias", _vp), ("k_bias", _vp), ("d_skip", _vp),
         ("ssm", _vp), ("state_k", _vp), ("state_v", _vp), ("phi", _vp),
         ("y", _vp),
+        ("scalar_dtype", _i32), ("q_norm_w", _vp), ("k_norm_w", _vp), ("norm_eps", _f32),
     ]
 
 

@@ -23,7 +23,8 @@ def _prep_state(state: SISOState) -> SISOState:
 
 
 def _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, raw, a_floor,
-            adt=None, dt=None, lam=None, dt_raw=None, a_raw=None, trap_raw=None, dt_bias=None, y=None):
+            adt=None, dt=None, lam=None, dt_raw=None, a_raw=None, trap_raw=None, dt_bias=None, y=None,
+            q_norm_w=None, k_norm_w=None, norm_eps=1e-5):
     T.require_cuda(q, k, v)
     bsz, n = q.shape
     h, p = v.shape[1], v.shape[2]
@@ -35,7 +36,11 @@ def _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, raw
         z = None if z is None else z.contiguous()
     if q.stride(0) != k.stride(0):
         q, k = q.contiguous(), k.contiguous()
-    angles = T.f32c(angles)
+    # bf16 scalar streams (the in_proj columns of a bf16 model) are read as they are
+    scal = (dt_raw, a_raw, trap_raw, angles) if raw else (adt, dt, lam, angles)
+    sbf = raw and all(t.dtype == torch.bfloat16 and t.stride(-1) == 1 for t in scal)
+    if not sbf:
+        angles = T.f32c(angles)
     st = _prep_state(state)
     if y is None:
         y = torch.empty(bsz, h, p, dtype=dt_io, device=q.device)
@@ -48,8 +53,14 @@ def _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, raw
     a.q, a.k, a.qk_stride_b = T.ptr(q), T.ptr(k), q.stride(0)
     a.v, a.z, a.vz_stride_b = T.ptr(v), T.ptr(z), v.stride(0)
     keep = []
+    a.scalar_dtype = C.M3_DTYPE_BF16 if sbf else C.M3_DTYPE_F32
+    if q_norm_w is not None:
+        qn, kn = T.f32dense(q_norm_w), T.f32dense(k_norm_w)
+        keep += [qn, kn]
+        a.q_norm_w, a.k_norm_w, a.norm_eps = T.ptr(qn), T.ptr(kn), norm_eps
     if raw:
-        dt_raw, a_raw, trap_raw = (T.f32c(t) for t in (dt_raw, a_raw, trap_raw))
+        if not sbf:
+            dt_raw, a_raw, trap_raw = (T.f32c(t) for t in (dt_raw, a_raw, trap_raw))
         if dt_raw.stride(0) != a_raw.stride(0) or dt_raw.stride(0) != trap_raw.stride(0):
             dt_raw, a_raw, trap_raw = dt_raw.contiguous(), a_raw.contiguous(), trap_raw.contiguous()
         dtb = T.f32dense(dt_bias)
@@ -83,11 +94,15 @@ siso_decode_folded = siso_decode
 
 
 def siso_decode_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, state: SISOState,
-                    d_skip=None, z=None, a_floor: float = 1e-4, dtype_policy: str = "bf16", y=None):
+                    d_skip=None, z=None, a_floor: float = 1e-4, dtype_policy: str = "bf16", y=None,
+                    q_norm_w=None, k_norm_w=None, norm_eps: float = 1e-5):
     """Decode step with ``lm_decode_step``'s length-1 preprocess fused
-    (``model.py:274-277``): raw ``(B, H)`` dt/A/trap slices in."""
+    (``model.py:274-277``): raw ``(B, H)`` dt/A/trap slices in (fp32, or bf16 in_proj
+    columns as they are).  With ``q_norm_w`` / ``k_norm_w`` the q / k rows are the raw C / B
+    columns and the layer's RMS norms (``layer.py:190-198``) run inside the kernel."""
     return _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, True, a_floor,
-                   dt_raw=dt_raw, a_raw=a_raw, trap_raw=trap_raw, dt_bias=dt_bias, y=y)
+                   dt_raw=dt_raw, a_raw=a_raw, trap_raw=trap_raw, dt_bias=dt_bias, y=y,
+                   q_norm_w=q_norm_w, k_norm_w=k_norm_w, norm_eps=norm_eps)
 
 
 def decode_step(*args, folded: bool = True, **kw):

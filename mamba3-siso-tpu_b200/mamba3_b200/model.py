@@ -144,15 +144,21 @@ def lm_decode_step(params: LMParams, token: torch.Tensor, states: List[SISOState
         h = LY.rms_norm(x, blk.norm_gain, c.norm_eps)
         proj = torch.matmul(h, p.in_proj.to(h.dtype))
         z, xx, b, cc, _, _, _, _ = LY.split_in_proj(proj, c)
-        dt_raw, a_raw, trap_raw, angles = LY._scalar_streams(proj, c)
-        b = LY.rms_norm(b, p.b_norm_weight, c.norm_eps)
-        cc = LY.rms_norm(cc, p.c_norm_weight, c.norm_eps)
+        s0 = 2 * c.d_inner + 2 * c.d_state  # dt / A / trap / angle columns, read in place
+        hh = c.nheads
+        dt_raw, a_raw, trap_raw = proj[:, s0:s0 + hh], proj[:, s0 + hh:s0 + 2 * hh], proj[:, s0 + 2 * hh:s0 + 3 * hh]
+        angles = proj[:, s0 + 3 * hh:]
+        # the B / C norms run inside the decode kernel
         y, st = KD.siso_decode_raw(cc, b, xx, dt_raw, a_raw, trap_raw, angles, p.dt_bias, p.c_bias, p.b_bias,
-                                   states[i], d_skip=p.d_skip, z=z, a_floor=c.a_floor, dtype_policy=c.policy_name)
+                                   states[i], d_skip=p.d_skip, z=z, a_floor=c.a_floor, dtype_policy=c.policy_name,
+                                   q_norm_w=p.c_norm_weight, k_norm_w=p.b_norm_weight, norm_eps=c.norm_eps)
         out_states.append(st)
-        x = x + torch.matmul(y.reshape(y.shape[0], c.d_inner).to(x.dtype), p.out_proj.to(x.dtype))
+        # residual adds fused into the projections' GEMMs
+        x = torch.addmm(x, y.reshape(y.shape[0], c.d_inner).to(x.dtype), p.out_proj.to(x.dtype))
         if blk.mlp is not None:
-            x = x + gated_mlp(blk.mlp, LY.rms_norm(x, blk.mlp_norm_gain, c.norm_eps))
+            hm = torch.matmul(LY.rms_norm(x, blk.mlp_norm_gain, c.norm_eps), blk.mlp.fc1.to(x.dtype))
+            value, gate = hm.chunk(2, dim=-1)
+            x = torch.addmm(x, value * F.silu(gate), blk.mlp.fc2.to(x.dtype))
     x = LY.rms_norm(x, params.final_norm, c.norm_eps)
     head = params.embed.t() if cfg.tie_head else params.head
     return torch.matmul(x, head.to(x.dtype)), out_states

@@ -113,3 +113,42 @@ def test_chain_equals_prefill_and_handoff():
         ys.append(y)
     y_all = torch.cat([o1.y, torch.stack(ys, 2)], dim=2)
     assert rel_error(y_all, y_pre) < 2e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(4, 8, 128, 64, 32), (3, 4, 32, 32, 8)])
+def test_fused_norms_and_inproj_columns(dtype, shape):
+    """The decode step as `model.lm_decode_step` drives it: raw C / B columns normalised in
+    the kernel and the dt / A / trap / angle columns of one in_proj row read in place
+    (bf16 in a bf16 model), against the layer's own RMS norm + fp32 columns."""
+    from mamba3_b200 import kernel_decode as KD
+    from mamba3_b200 import layer as LY
+    from mamba3_b200.state import SISOState
+
+    b, h, n, p, nr = shape
+    g = torch.Generator(device="cuda").manual_seed(3)
+    r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    width = 2 * h * p + 2 * n + 3 * h + nr
+    proj = (r(b, width) * 0.7).to(dtype)
+    s0 = 2 * h * p + 2 * n
+    z, xx = proj[:, :h * p].view(b, h, p), proj[:, h * p:2 * h * p].view(b, h, p)
+    kb, qc = proj[:, 2 * h * p:2 * h * p + n], proj[:, 2 * h * p + n:s0]
+    cols = [proj[:, s0:s0 + h], proj[:, s0 + h:s0 + 2 * h], proj[:, s0 + 2 * h:s0 + 3 * h], proj[:, s0 + 3 * h:]]
+    wq, wk = 1 + 0.1 * r(n), 1 + 0.1 * r(n)
+    dtb, qb, kbias, dsk = 0.3 * r(h), 0.1 * r(h, n), 0.1 * r(h, n), r(h)
+
+    def state():
+        gs = torch.Generator(device="cuda").manual_seed(4)
+        rs = lambda *s: torch.randn(*s, device="cuda", generator=gs)
+        return SISOState(ssm=rs(b, h, p, n) * 0.3, k=rs(b, h, n), v=rs(b, h, p), phi=rs(b, h, nr).abs())
+
+    s1, s2 = state(), state()
+    y1, _ = KD.siso_decode_raw(qc, kb, xx, *cols, dtb, qb, kbias, s1, d_skip=dsk, z=z, q_norm_w=wq, k_norm_w=wk,
+                               norm_eps=1e-5, dtype_policy="f32" if dtype == torch.float32 else "bf16")
+    qn, kn = LY.rms_norm(qc, wq, 1e-5), LY.rms_norm(kb, wk, 1e-5)
+    y2, _ = KD.siso_decode_raw(qn, kn, xx, *(c.float() for c in cols), dtb, qb, kbias, s2, d_skip=dsk, z=z,
+                               dtype_policy="f32" if dtype == torch.float32 else "bf16")
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert rel_error(y1, y2) < tol
+    for name, a, c in zip(("ssm", "k", "v", "phi"), s1, s2):
+        assert rel_error(a, c) < tol, name
