@@ -4,8 +4,8 @@
 
 namespace m3 {
 
-template <int N, int P, typename T, bool MMB>
-static int run_decode(const M3DecodeArgs& a, cudaStream_t s) {
+template <int N, int P, typename T, bool MMB, bool FUSED>
+static int run_decode_v(const M3DecodeArgs& a, cudaStream_t s) {
   int dev = 0;
   cudaGetDevice(&dev);
   static int sms[64] = {};
@@ -13,15 +13,21 @@ static int run_decode(const M3DecodeArgs& a, cudaStream_t s) {
   if (dev < 0 || dev >= 64) return set_error(M3_ERR_LAUNCH, "device index out of range");
   if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   if (!attr[dev]) {
-    if (cudaFuncSetAttribute(decode_kernel<N, P, T, MMB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(decode_kernel<N, P, T, MMB, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)DecSmem<N, P>::kBytes) != cudaSuccess)
       return check_launch("m3_siso_decode: cudaFuncSetAttribute");
     attr[dev] = true;
   }
   const int items = a.batch * a.nheads;
   const int grid = items < sms[dev] * kDecCtasPerSm ? items : sms[dev] * kDecCtasPerSm;
-  decode_kernel<N, P, T, MMB><<<grid, kDecThreads, DecSmem<N, P>::kBytes, s>>>(a);
+  decode_kernel<N, P, T, MMB, FUSED><<<grid, kDecThreads, DecSmem<N, P>::kBytes, s>>>(a);
   return check_launch("m3_siso_decode");
+}
+
+template <int N, int P, typename T, bool MMB>
+static int run_decode(const M3DecodeArgs& a, cudaStream_t s) {
+  const bool fused = a.q_norm_w != nullptr || a.scalar_dtype == M3_DTYPE_BF16;
+  return fused ? run_decode_v<N, P, T, MMB, true>(a, s) : run_decode_v<N, P, T, MMB, false>(a, s);
 }
 
 int read_decode_error(int reset) {

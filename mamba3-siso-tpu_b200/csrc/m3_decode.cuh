@@ -64,7 +64,9 @@ struct DecSmem {
   static constexpr size_t kBytes = 2 * (size_t)kStateBytes;  // the two state buffers (dynamic)
 };
 
-template <int N, int P, typename T, bool MMB>
+// FUSED: the lm_decode_step variant (in-kernel B / C norms, bf16 scalar streams); the plain
+// variant compiles both out, so the standalone decode keeps its shorter preamble.
+template <int N, int P, typename T, bool MMB, bool FUSED>
 __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(const M3DecodeArgs a) {
   static_assert(N <= 128 && P <= 128 && N % 4 == 0 && (P * N / 4) % 32 == 0, "decode tiling");
   constexpr int LPR = N / 4;              // lanes (float4 columns) per state row
@@ -99,17 +101,18 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
   // latency overlaps the previous item's update.
   struct In {
     float dtr, ar, trr;       // raw dt / A / trap (or adt / dt / lam)
-    float u, w, um, wm, kpv;  // column threads: q, k, their pair partners (biases not yet added), k_prev
+    float u, w, um, wm, kpv;  // column threads: q, k, their pair partners, k_prev
+    float bq, bk, bqm, bkm;   // the biases of those columns (added after the fused norm)
     float ph, an;             // angle threads: phi, raw angle
     float vc, vp, zz;         // row threads: v, v_prev, z
   };
   const int n = tid, j = n < H2 ? n : n - H2;
   const int mm = n < H2 ? n + H2 : n - H2;  // the pair partner
-  const bool sbf = a.scalar_dtype == M3_DTYPE_BF16;
+  const bool sbf = FUSED && a.scalar_dtype == M3_DTYPE_BF16;
   auto lds = [&](const float* p, size_t i) {  // a scalar-stream element in scalar_dtype
     return sbf ? ld(reinterpret_cast<const __nv_bfloat16*>(p) + i) : p[i];
   };
-  const bool fnorm = a.q_norm_w != nullptr;
+  const bool fnorm = FUSED && a.q_norm_w != nullptr;
   auto load_in = [&](int item, In& x) {
     const int b = item / H, h = item % H;
     const size_t bh = (size_t)item;
@@ -128,9 +131,13 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
       const T* k = (const T*)a.k + (size_t)b * a.qk_stride_b;
       x.u = ld(q + n);
       x.w = ld(k + n);
+      x.bq = a.q_bias[h * N + n];
+      x.bk = a.k_bias[h * N + n];
       if (j < Nr) {
         x.um = ld(q + mm);
         x.wm = ld(k + mm);
+        x.bqm = a.q_bias[h * N + mm];
+        x.bkm = a.k_bias[h * N + mm];
       }
       x.kpv = a.state_k[bh * N + n];
     }
@@ -211,11 +218,11 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtasPerSm) decode_kernel(cons
           wm = rnd_io<T>(wm * rk * a.k_norm_w[mm]);
         }
       }
-      u += a.q_bias[h * N + n];
-      w += a.k_bias[h * N + n];
+      u += cur.bq;
+      w += cur.bk;
       if (j < Nr) {
-        um += a.q_bias[h * N + mm];
-        wm += a.k_bias[h * N + mm];
+        um += cur.bqm;
+        wm += cur.bkm;
       }
       float qv = u, kv = w;
       if (j < Nr) {
