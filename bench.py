@@ -412,9 +412,64 @@ def bench_decode(steps, warmup, world, rank, peaks, batch=256):
     kper = kms / (steps * 4)
     byts = batch * H * (2 * P * N * 4 + 2 * (N + P) * 4 + 2 * Nr * 4 + 3 * P * 2 + 3 * 4)
     gbs = byts / (kper / 1e3) / 1e9
+    gen = bench_generate(params, cfg, rank)
     return {"us_per_token": per * 1e3 / batch, "ms_per_step": per, "batch_per_gpu": batch,
             "kernel_ms_per_layer": kper, "kernel_gbs": gbs, "kernel_hbm_frac": gbs / peaks["hbm_gbs"],
-            "kernel_bytes_per_layer": byts, "launches_per_step": cfg.n_layers}
+            "kernel_bytes_per_layer": byts, "launches_per_step": cfg.n_layers, "generate_b1": gen}
+
+
+def bench_generate(params, cfg, rank, n_short=32, n_long=160, reps=3):
+    """`train.generate` at B = 1 on the configs[3] model (``train.py:503-582``): a 129-token
+    prompt (128 prefilled in one chunk), sampling on the device.  Per-token cost = the
+    difference of two generation lengths (best of ``reps`` each), so prefill and set-up
+    cancel; device loop (one replayed CUDA graph per token, host sync every 32 tokens) and
+    eager launches.  ``graph_step_ms`` is the device time of one replay (CUDA events)."""
+    from mamba3_b200 import model as M
+    from mamba3_b200 import train as TR
+    from mamba3_b200.sampling import TokenSampler
+
+    g = torch.Generator().manual_seed(5000 + rank)
+    prompt = torch.randint(0, cfg.vocab_size, (129,), generator=g).tolist()
+    res = {}
+    for name, dl in (("device_loop", True), ("eager", False)):
+        times = {}
+        for n in (n_short, n_long):
+            best = float("inf")
+            for _ in range(reps):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                TR.generate(params, cfg, 1, prompt, n_tokens=n, device_loop=dl)
+                torch.cuda.synchronize()
+                best = min(best, time.perf_counter() - t0)
+            times[n] = best
+        res[name + "_us_per_token"] = (times[n_long] - times[n_short]) / (n_long - n_short) * 1e6
+    states = M.zero_states(cfg, 1)
+    smp = TokenSampler(1, cfg.vocab_size, "cuda")
+    smp.reset([prompt])
+    graph = TR._GenerateGraph(params, cfg, states, smp, None)
+    res["graph_step_ms"] = timed(graph.replay, 32, 3, 1) / 32
+    res["timing"] = "host wall clock around whole generate calls (host syncs included); graph_step_ms by CUDA events"
+    return res
+
+
+def bench_seqpar(c, steps, warmup, world, rank):
+    """Sequence-parallel prefill of configs[1]'s batch: rank r scans the r-th L / world
+    slice (`siso.siso_segment_seq_parallel`, two scans + two all-gathers).  The forward
+    section's ms_per_step is one GPU scanning the same B x L."""
+    from mamba3_b200 import siso as SISO
+
+    L = c["L"]
+    per = L // world
+    d = make_cfg2_inputs(c, seed=7000)  # the same sequences on every rank
+    lo, hi = rank * per, (rank + 1) * per
+    args = (d["q"][:, lo:hi], d["k"][:, lo:hi], d["x"][:, lo:hi].permute(0, 2, 1, 3), d["dt_raw"][:, lo:hi],
+            d["a_raw"][:, lo:hi], d["trap_raw"][:, lo:hi], d["angles"][:, lo:hi], d["dt_bias"], d["q_bias"],
+            d["k_bias"], d["d_skip"], d["z"][:, lo:hi].permute(0, 2, 1, 3))
+    ms = timed(lambda: SISO.siso_segment_seq_parallel(*args, chunk=c["chunk"], policy_name="bf16"),
+               steps, warmup, world)
+    tok = c["B"] * L
+    return {"tok_s": tok / (ms / steps / 1e3), "ms_per_step": ms / steps, "slice_len": per,
+            "note": "one batch of B sequences split along L over the ranks (strong scaling of one prefill)"}
 
 
 def cpu_baseline_sample(threads=None, seconds=10.0):
@@ -509,6 +564,28 @@ def run_profile_case(which):
                 torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         return 0
+    if which == "generate":  # configs[3] model, B = 1: one decode step + sampling, eager, in an NVTX range
+        from mamba3_b200 import layer as LY
+        from mamba3_b200 import model as M
+        from mamba3_b200.sampling import TokenSampler
+
+        scfg = LY.SISOConfig(d_model=2048, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                             policy_name="bf16")
+        cfg = M.LMConfig(vocab_size=128256, n_layers=24, siso=scfg, d_intermediate=4096)
+        params = M.init_lm(cfg, key=0, dtype=torch.bfloat16)
+        states = M.zero_states(cfg, 1)
+        smp = TokenSampler(1, cfg.vocab_size, "cuda")
+        smp.reset([[1, 2, 3]])
+        with torch.no_grad():
+            for i in range(3):
+                if i == 2:
+                    torch.cuda.nvtx.range_push("generate_token")
+                lg, _ = M.lm_decode_step(params, smp.token, states, cfg)
+                smp.pick(lg)
+                if i == 2:
+                    torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        return 0
     if which == "decodestep":  # configs[3]: one 24-layer decode step, eager, inside an NVTX range
         from mamba3_b200 import layer as LY
         from mamba3_b200 import model as M
@@ -567,8 +644,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--what", default="all", help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep", "trainstep"],
+    ap.add_argument("--what", default="all",
+                    help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu,seqpar (N > 1) or all")
+    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep", "trainstep", "generate"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()
@@ -581,7 +659,7 @@ def main():
     if args.impl == "reference":
         return run_reference(args, world, rank)
 
-    what = set(["fwd", "e2e", "fwdbwd", "decode", "train", "layer", "cpu"] if args.what == "all"
+    what = set(["fwd", "e2e", "fwdbwd", "decode", "train", "layer", "cpu", "seqpar"] if args.what == "all"
                else args.what.split(","))
     peaks = load_peaks()
     traffic = load_traffic()
@@ -600,6 +678,8 @@ def main():
             out["train"] = bench_train(max(2, args.steps // 3), args.warmup, world, rank)
         if "layer" in what:
             out["layer_cfg0"] = bench_layer_cfg0(args.steps, args.warmup, world)
+        if "seqpar" in what and world > 1:
+            out["seqpar"] = bench_seqpar(c, max(2, args.steps // 2), args.warmup, world, rank)
     clocks = clk.summary()
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
 
@@ -647,6 +727,8 @@ def main():
         line["train"] = out["train"]
     if "layer_cfg0" in out:
         line["layer_cfg0"] = out["layer_cfg0"]
+    if "seqpar" in out:
+        line["seqpar_prefill"] = out["seqpar"]
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
