@@ -232,6 +232,30 @@ int m3_rms_norm_bwd(const void *x, int64_t x_row_stride, const void *weight, con
                     int32_t x_dtype, int32_t w_dtype, void *stream);
 
 /* ---------------------------------------------------------------------------------
+ * Small-batch projection of the decode step (model.py:244-296 at batch <= 8):
+ *   out (m, n) = f(x) @ w (+ residual),  w bf16 (k, n) row-major, x / residual / out bf16,
+ * with f chosen by x_mode: 0 identity; 1 RMS norm of each x row times norm_w (layer.py:190-198,
+ * fp32 math rounded to bf16); 2 value * silu(gate) with value / gate the two k-halves of a
+ * 2k-wide x row (model.py:125-137).  residual (optional) is added before the one rounding
+ * (torch.addmm's).  Workspace: scratch of m3_gemv_scratch_floats(m, k, n) floats and
+ * tickets of (n + 255) / 256 ints that must be zero before the first call (each call leaves
+ * them zero).  Deterministic.  m <= 8; every leading dimension and n multiples of 8.
+ * ------------------------------------------------------------------------------- */
+typedef struct M3GemvArgs {
+  int32_t m, k, n, x_mode;
+  const void *x;       int64_t x_ld;
+  const float *norm_w; float eps;
+  const void *w;       int64_t w_ld;
+  const void *residual; int64_t r_ld;
+  void *out;           int64_t out_ld;
+  float *scratch;
+  int32_t *tickets;
+} M3GemvArgs;
+
+int m3_gemv_bf16(const M3GemvArgs *args, void *stream);
+size_t m3_gemv_scratch_floats(int32_t m, int32_t k, int32_t n);
+
+/* ---------------------------------------------------------------------------------
  * Token sampling for generation (mamba3_pallas/train.py:454-500 `_pick_token`, and the
  * window bookkeeping of train.py:559-579): per row, logits -> repetition penalty on the
  * ids whose `seen_count` is > 0 (l / rep_penalty if l > 0 else l * rep_penalty), divide by

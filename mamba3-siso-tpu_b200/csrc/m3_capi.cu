@@ -131,6 +131,25 @@ int m3_copy2d_async(void* dst, size_t dpitch, const void* src, size_t spitch, si
   return M3_OK;
 }
 
+size_t m3_gemv_scratch_floats(int32_t m, int32_t k, int32_t n) {
+  if (m <= 0 || k <= 0 || n <= 0) return 0;
+  const int mp = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+  return (size_t)m3::gemv_ksplit(m, k, n) * mp * n;
+}
+
+int m3_gemv_bf16(const M3GemvArgs* args, void* stream) {
+  if (!args) return m3::set_error(M3_ERR_ARG, "m3_gemv_bf16: args is NULL");
+  const M3GemvArgs& a = *args;
+  if (!a.x || !a.w || !a.out || !a.scratch || !a.tickets || (a.x_mode == 1 && !a.norm_w))
+    return m3::set_error(M3_ERR_ARG, "m3_gemv_bf16: NULL pointer");
+  if (a.m <= 0 || a.m > 8 || a.k <= 0 || a.n <= 0 || a.n % 8 || a.w_ld % 8 || a.w_ld < a.n || a.out_ld < a.n ||
+      a.x_ld < (a.x_mode == 2 ? 2 * (int64_t)a.k : a.k) || (a.residual && a.r_ld < a.n))
+    return m3::set_error(M3_ERR_SHAPE, "m3_gemv_bf16: bad m (1..8) / k / n (multiple of 8) / leading dimensions");
+  if (a.x_mode < 0 || a.x_mode > 2) return m3::set_error(M3_ERR_ARG, "m3_gemv_bf16: x_mode must be 0, 1 or 2");
+  if (((uintptr_t)a.w) % 16) return m3::set_error(M3_ERR_ARG, "m3_gemv_bf16: w must be 16-byte aligned");
+  return m3::launch_gemv(a, (cudaStream_t)stream);
+}
+
 int m3_sample_tokens(const M3SampleArgs* args, void* stream) {
   if (!args) return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: args is NULL");
   const M3SampleArgs& a = *args;

@@ -109,9 +109,18 @@ class M3SampleArgs(ctypes.Structure):
     ]
 
 
+class M3GemvArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", _i32), ("k", _i32), ("n", _i32), ("x_mode", _i32), ("x", _vp), ("x_ld", _i64),
+        ("norm_w", _vp), ("eps", _f32), ("w", _vp), ("w_ld", _i64), ("residual", _vp), ("r_ld", _i64),
+        ("out", _vp), ("out_ld", _i64), ("scratch", _vp), ("tickets", _vp),
+    ]
+
+
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
-           "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens")
+           "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
+           "m3_gemv_scratch_floats")
 
 _lib = None
 
@@ -141,6 +150,10 @@ def lib():
         L.m3_device_error.restype = ctypes.c_int
         L.m3_sample_tokens.argtypes = [ctypes.POINTER(M3SampleArgs), _vp]
         L.m3_sample_tokens.restype = ctypes.c_int
+        L.m3_gemv_bf16.argtypes = [ctypes.POINTER(M3GemvArgs), _vp]
+        L.m3_gemv_bf16.restype = ctypes.c_int
+        L.m3_gemv_scratch_floats.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+        L.m3_gemv_scratch_floats.restype = ctypes.c_size_t
         L.m3_copy2d_async.argtypes = [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]
         L.m3_copy2d_async.restype = ctypes.c_int
         L.m3_rms_norm.argtypes = [_vp, ctypes.c_int64, _vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,

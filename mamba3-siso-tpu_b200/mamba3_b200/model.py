@@ -16,6 +16,7 @@ import torch.nn.functional as F
 
 from . import kernel_decode as KD
 from . import layer as LY
+from . import projection as PJ
 from .state import SISOState, zero_state
 
 
@@ -139,10 +140,14 @@ def lm_decode_step(params: LMParams, token: torch.Tensor, states: List[SISOState
     if compute_dtype is not None:
         x = x.to(compute_dtype)
     out_states = []
+    small = PJ.eligible(x, params.blocks[0].siso.in_proj) if params.blocks else False
     for i, blk in enumerate(params.blocks):
         p = blk.siso
-        h = LY.rms_norm(x, blk.norm_gain, c.norm_eps)
-        proj = torch.matmul(h, p.in_proj.to(h.dtype))
+        if small:  # batch <= 8, bf16: W streamed by m3_gemv_bf16 with the norm folded in
+            proj = PJ.small_proj(x, p.in_proj, norm_w=blk.norm_gain, eps=c.norm_eps)
+        else:
+            h = LY.rms_norm(x, blk.norm_gain, c.norm_eps)
+            proj = torch.matmul(h, p.in_proj.to(h.dtype))
         z, xx, b, cc, _, _, _, _ = LY.split_in_proj(proj, c)
         s0 = 2 * c.d_inner + 2 * c.d_state  # dt / A / trap / angle columns, read in place
         hh = c.nheads
@@ -153,12 +158,20 @@ def lm_decode_step(params: LMParams, token: torch.Tensor, states: List[SISOState
                                    states[i], d_skip=p.d_skip, z=z, a_floor=c.a_floor, dtype_policy=c.policy_name,
                                    q_norm_w=p.c_norm_weight, k_norm_w=p.b_norm_weight, norm_eps=c.norm_eps)
         out_states.append(st)
-        # residual adds fused into the projections' GEMMs
-        x = torch.addmm(x, y.reshape(y.shape[0], c.d_inner).to(x.dtype), p.out_proj.to(x.dtype))
+        # residual adds fused into the projections
+        y2 = y.reshape(y.shape[0], c.d_inner).to(x.dtype)
+        if small:
+            x = PJ.small_proj(y2, p.out_proj, residual=x)
+        else:
+            x = torch.addmm(x, y2, p.out_proj.to(x.dtype))
         if blk.mlp is not None:
-            hm = torch.matmul(LY.rms_norm(x, blk.mlp_norm_gain, c.norm_eps), blk.mlp.fc1.to(x.dtype))
-            value, gate = hm.chunk(2, dim=-1)
-            x = torch.addmm(x, value * F.silu(gate), blk.mlp.fc2.to(x.dtype))
+            if small:
+                hm = PJ.small_proj(x, blk.mlp.fc1, norm_w=blk.mlp_norm_gain, eps=c.norm_eps)
+                x = PJ.small_proj(hm, blk.mlp.fc2, silu_gate=True, residual=x)
+            else:
+                hm = torch.matmul(LY.rms_norm(x, blk.mlp_norm_gain, c.norm_eps), blk.mlp.fc1.to(x.dtype))
+                value, gate = hm.chunk(2, dim=-1)
+                x = torch.addmm(x, value * F.silu(gate), blk.mlp.fc2.to(x.dtype))
     x = LY.rms_norm(x, params.final_norm, c.norm_eps)
     head = params.embed.t() if cfg.tie_head else params.head
     return torch.matmul(x, head.to(x.dtype)), out_states
