@@ -292,18 +292,25 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
     z = d["z"].permute(0, 2, 1, 3)
     dy = d["dy"].permute(0, 2, 1, 3)
 
-    def step():
-        fwd_call(d, c)
+    from mamba3_b200 import kernel_fwd as KF
+
+    def step():  # the forward saves the chunk-start states into the backward's workspace
+        _, saved = KF.siso_forward_raw(d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                                       d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z,
+                                       chunk=c["chunk"], dtype_policy="bf16", bwd_states=ws, return_saved=True)
         KB.siso_backward_raw(dy, d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
                              d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z, chunk=c["chunk"],
-                             dtype_policy="bf16", workspace=ws)
+                             dtype_policy="bf16", workspace=ws, states_ready=saved)
+        return saved
 
+    saved = step()
     ms = timed(step, steps, warmup, world)
     per = ms / steps
     th = c["B"] * c["L"] * c["H"]
     flops = (FWD_FLOP_PER_TOKEN_HEAD + BWD_FLOP_PER_TOKEN_HEAD) * th
     return {"tok_s": c["B"] * c["L"] * world / (per / 1e3), "ms_per_step": per,
-            "tflops": flops / (per / 1e3) / 1e12, "launches_per_step": 3}  # fwd, states sweep, bwd
+            "tflops": flops / (per / 1e3) / 1e12,
+            "launches_per_step": 2 if saved else 3}  # fwd (saving the states) + bwd; else + the recompute sweep
 
 
 def bench_layer_cfg0(steps, warmup, world):

@@ -100,6 +100,13 @@ typedef struct M3FwdArgs {
   int32_t chunk_states_dtype;           /* M3_DTYPE_* of chunk_states */
 
   int32_t kernel;                       /* M3_KERNEL_*: 0 = pick automatically */
+
+  /* Optional: the workspace of a later m3_siso_bwd on the same inputs and seeds.  When the
+   * forward runs on tensor cores (m3_siso_fwd_saves_states() == 1) it also writes there the
+   * chunk-start states the backward would otherwise recompute; that backward then sets
+   * states_ready.  bwd_states_bytes >= m3_siso_bwd_workspace_size(&dims). */
+  void *bwd_states;
+  size_t bwd_states_bytes;
 } M3FwdArgs;
 
 /* Kernel selection for m3_siso_fwd / m3_siso_bwd.  AUTO uses the tcgen05 tensor-core kernel where it
@@ -109,6 +116,8 @@ typedef struct M3FwdArgs {
 enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2 };
 
 int m3_siso_fwd(const M3FwdArgs *args, void *stream);
+/* 1 if m3_siso_fwd(args) takes the tensor-core path and so fills bwd_states, else 0. */
+int m3_siso_fwd_saves_states(const M3FwdArgs *args);
 
 /* ---------------------------------------------------------------------------------
  * Backward.  Replaces kernel_bwd.siso_backward (mamba3_pallas/kernel_bwd.py:534-669;
@@ -152,6 +161,9 @@ typedef struct M3BwdArgs {
   size_t workspace_bytes;
 
   int32_t kernel;                         /* M3_KERNEL_*: 0 = pick automatically */
+  int32_t states_ready;                   /* 1: `workspace` was passed as bwd_states to an
+                                             m3_siso_fwd on these inputs that saved them: the
+                                             tensor-core backward skips its recompute sweep */
 } M3BwdArgs;
 
 size_t m3_siso_bwd_workspace_size(const M3Dims *dims);

@@ -175,6 +175,24 @@ int m3_device_error(int reset) {
   return f != 0 ? f : d;
 }
 
+static void fwd_defaults(M3FwdArgs& a) {
+  def_blx(a.q_st, a.dims, a.dims.state_dim);
+  def_blx(a.k_st, a.dims, a.dims.state_dim);
+  def_bhlp(a.v_st, a.dims);
+  def_bhlp(a.z_st, a.dims);
+  def_bhlp(a.y_st, a.dims);
+  def_blh(a.raw_st, a.dims);
+  def_blx(a.ang_st, a.dims, a.dims.n_angles);
+}
+
+int m3_siso_fwd_saves_states(const M3FwdArgs* args) {
+  if (!args) return 0;
+  M3FwdArgs a = *args;
+  if (check_enums(a.io_dtype, a.policy) != M3_OK || check_dims(a.dims, 64) != M3_OK) return 0;
+  fwd_defaults(a);
+  return fwd_saves_states(a) ? 1 : 0;
+}
+
 int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   g_err.clear();
   if (!args) return set_error(M3_ERR_ARG, "args is NULL");
@@ -187,15 +205,13 @@ int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
     return set_error(M3_ERR_ARG, "y, final_ssm, final_k, final_v are required");
   if (a.chunk_states && a.chunk_states_dtype != M3_DTYPE_F32 && a.chunk_states_dtype != M3_DTYPE_BF16)
     return set_error(M3_ERR_ARG, "chunk_states_dtype must be F32 or BF16");
-  def_blx(a.q_st, a.dims, a.dims.state_dim);
-  def_blx(a.k_st, a.dims, a.dims.state_dim);
-  def_bhlp(a.v_st, a.dims);
-  def_bhlp(a.z_st, a.dims);
-  def_bhlp(a.y_st, a.dims);
-  def_blh(a.raw_st, a.dims);
-  def_blx(a.ang_st, a.dims, a.dims.n_angles);
+  fwd_defaults(a);
   if (a.kernel < M3_KERNEL_AUTO || a.kernel > M3_KERNEL_TENSORCORE)
     return set_error(M3_ERR_ARG, "kernel must be AUTO, GENERIC or TENSORCORE");
+  if (a.bwd_states && a.bwd_states_bytes < bwd_workspace_bytes(a.dims))
+    return set_error(M3_ERR_WORKSPACE, "bwd_states is smaller than m3_siso_bwd_workspace_size");
+  if (a.bwd_states && ((uintptr_t)a.bwd_states) % 256 != 0)
+    return set_error(M3_ERR_ARG, "bwd_states must be 256-byte aligned");
   return launch_fwd(a, (cudaStream_t)stream);
 }
 

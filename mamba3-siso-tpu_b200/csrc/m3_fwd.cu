@@ -45,7 +45,11 @@ static bool fwd_tc_eligible(const M3FwdArgs& a) {
   return true;
 }
 
-static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s, const tc::TcStates* states = nullptr) {
+static size_t tc_tiles_bytes(const M3Dims& d);
+
+// `states`: the states-only sweep; `save`: a full forward that also writes them
+static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s, const tc::TcStates* states = nullptr,
+                      const tc::TcStates* save = nullptr) {
   const int mode = (a.raw ? 1 : 0) + (states ? 2 : 0);
   decltype(&tc::fwd_tc_kernel<true, false>) kerns[4] = {tc::fwd_tc_kernel<false, false>, tc::fwd_tc_kernel<true, false>,
                                                          tc::fwd_tc_kernel<false, true>, tc::fwd_tc_kernel<true, true>};
@@ -59,7 +63,8 @@ static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s, const tc::TcStates* st
     attr_done[mode][dev] = true;
   }
   const int nseq = a.dims.batch * a.dims.nheads;
-  kern<<<(nseq + 1) / 2, tc::kThreads, tc::kSmemBytes, s>>>(a, states ? *states : tc::TcStates{nullptr, nullptr});
+  const tc::TcStates so = states ? *states : save ? *save : tc::TcStates{nullptr, nullptr};
+  kern<<<(nseq + 1) / 2, tc::kThreads, tc::kSmemBytes, s>>>(a, so);
   return check_launch("m3_siso_fwd (tensor core)");
 }
 
@@ -70,6 +75,7 @@ int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaSt
 }
 
 bool fwd_tc_eligible_public(const M3FwdArgs& a) { return fwd_tc_eligible(a); }
+bool fwd_saves_states(const M3FwdArgs& a) { return a.kernel != M3_KERNEL_GENERIC && fwd_tc_eligible(a); }
 
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   const bool tc_ok = fwd_tc_eligible(a);
@@ -77,7 +83,14 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
     return set_error(M3_ERR_UNSUPPORTED,
                      "tensor-core forward needs bf16 I/O, bf16 policy, N=128, P=64, chunk % 128 == 0, "
                      "n_angles a multiple of 8 and <= 64, and 16-byte aligned rows");
-  if (tc_ok && a.kernel != M3_KERNEL_GENERIC) return run_fwd_tc(a, s);
+  if (tc_ok && a.kernel != M3_KERNEL_GENERIC) {
+    if (a.bwd_states) {  // the backward workspace's state region: tiles, then angle carries
+      uint8_t* ws = (uint8_t*)a.bwd_states;
+      const tc::TcStates save{ws, (float*)(ws + tc_tiles_bytes(a.dims))};
+      return run_fwd_tc(a, s, nullptr, &save);
+    }
+    return run_fwd_tc(a, s);
+  }
   const bool mmb = a.policy == M3_POLICY_BF16;
   const bool bf = a.io_dtype == M3_DTYPE_BF16;
 #define X(N_, P_)                                                                  \
@@ -88,7 +101,7 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
 }
 
 // ---- backward on tensor cores ------------------------------------------------------------
-static size_t tc_tiles_bytes(const M3Dims& d) {
+static size_t tc_tiles_bytes(const M3Dims& d) {  // also the offset of the angle carries
   return (size_t)d.batch * d.nheads * (d.seqlen / tc::kC + 1) * 16384u;
 }
 static size_t tc_phis_bytes(const M3Dims& d) {
@@ -139,8 +152,10 @@ int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s) {
   f.q_bias = a.q_bias; f.k_bias = a.k_bias; f.d_skip = a.d_skip;
   f.seed_ssm = a.seed_ssm; f.seed_k = a.seed_k; f.seed_v = a.seed_v; f.seed_phi = a.seed_phi;
   f.seed_coef = a.seed_coef;
-  int rc = launch_fwd_states_tc(f, tiles, phis, s);
-  if (rc != M3_OK) return rc;
+  if (!a.states_ready) {  // else a forward on the same inputs already wrote them
+    const int rc = launch_fwd_states_tc(f, tiles, phis, s);
+    if (rc != M3_OK) return rc;
+  }
   if (a.seed_ssm) {
     cudaMemsetAsync(a.dseed_k, 0, (size_t)d.batch * d.nheads * d.state_dim * sizeof(float), s);
     cudaMemsetAsync(a.dseed_v, 0, (size_t)d.batch * d.nheads * d.headdim * sizeof(float), s);

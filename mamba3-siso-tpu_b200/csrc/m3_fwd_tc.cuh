@@ -112,7 +112,8 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
 
 // Outputs of the states-only mode used by the backward's recompute sweep: the bf16 state
 // tile image (the layout the backward's tensor-core operands use) at every chunk start
-// plus the final state, and the rotary-angle carry at every chunk start.
+// plus the final state, and the rotary-angle carry at every chunk start.  A full forward
+// given them writes the same (so a backward on the same inputs can skip its sweep).
 struct TcStates {
   uint8_t* tiles;  // (B*H, nchunk + 1, 16 KB)
   float* phis;     // (B*H, nchunk, Nr)
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
     for (int c = 0; c < nchunk && ok; ++c) {
       const int t0 = c * kC;
       const int tg = t0 + t;  // this thread's token (row roles)
-      if constexpr (STATES) {
+      if (STATES || so.tiles) {  // states-only mode, or a forward saving them for the backward
         dump_state_tile(c);
         if (RAW && lane == 0 && 8 * lwarp < Nr)
 #pragma unroll
@@ -662,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       M3_TC_MARK(6);
     }
 
-    if constexpr (STATES) {
+    if (STATES || so.tiles) {
       slot_sync(slot);
       dump_state_tile(nchunk);
     }

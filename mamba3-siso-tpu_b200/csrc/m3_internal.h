@@ -27,6 +27,7 @@ int launch_rms_norm_bwd(const void* x, int64_t xs, const void* w, const float* r
                         cudaStream_t s);
 int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s);
 bool fwd_tc_eligible_public(const M3FwdArgs& a);
+bool fwd_saves_states(const M3FwdArgs& a);
 size_t bwd_tc_workspace_bytes(const M3Dims& d);
 bool bwd_tc_eligible(const M3BwdArgs& a);
 int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s);

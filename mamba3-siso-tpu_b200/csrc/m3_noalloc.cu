@@ -74,5 +74,6 @@ extern "C" int m3_siso_bwd_noalloc(const M3BwdArgs* args, void* stream) {
   M3BwdArgs a = *args;
   a.workspace = scratch;
   a.workspace_bytes = kNoAllocScratchBytes;
+  a.states_ready = 0;  // the library's own scratch never holds a forward's saved states
   return m3_siso_bwd(&a, stream);
 }

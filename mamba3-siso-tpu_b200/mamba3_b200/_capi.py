@@ -52,7 +52,7 @@ class M3FwdArgs(ctypes.Structure):
         ("y", _vp), ("y_st", M3Strides),
         ("final_ssm", _vp), ("final_k", _vp), ("final_v", _vp), ("final_phi", _vp),
         ("ybar", _vp), ("chunk_states", _vp), ("chunk_states_dtype", _i32),
-        ("kernel", _i32),
+        ("kernel", _i32), ("bwd_states", _vp), ("bwd_states_bytes", ctypes.c_size_t),
     ]
 
 
@@ -79,7 +79,7 @@ class M3BwdArgs(ctypes.Structure):
         ("dq_bias", _vp), ("dk_bias", _vp), ("dd_skip", _vp),
         ("dseed_ssm", _vp), ("dseed_k", _vp), ("dseed_v", _vp), ("dseed_coef", _vp), ("dseed_phi", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
-        ("kernel", _i32),
+        ("kernel", _i32), ("states_ready", _i32),
     ]
 
 
@@ -120,7 +120,7 @@ class M3GemvArgs(ctypes.Structure):
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
            "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
-           "m3_gemv_scratch_floats")
+           "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states")
 
 _lib = None
 
@@ -136,6 +136,8 @@ def lib():
         L = ctypes.CDLL(_LIB_PATH)
         L.m3_siso_fwd.argtypes = [ctypes.POINTER(M3FwdArgs), _vp]
         L.m3_siso_fwd.restype = ctypes.c_int
+        L.m3_siso_fwd_saves_states.argtypes = [ctypes.POINTER(M3FwdArgs)]
+        L.m3_siso_fwd_saves_states.restype = ctypes.c_int
         L.m3_siso_bwd.argtypes = [ctypes.POINTER(M3BwdArgs), _vp]
         L.m3_siso_bwd.restype = ctypes.c_int
         L.m3_siso_bwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]

@@ -137,7 +137,10 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
                       d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                       dfinal_ssm=None, dfinal_k=None, dfinal_v=None, dfinal_phi=None,
                       a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
-                      workspace=None, kernel: str = "auto") -> RawGrads:
+                      workspace=None, kernel: str = "auto", states_ready: bool = False) -> RawGrads:
+    """Gradients of the fused raw boundary.  ``states_ready``: ``workspace`` was given as
+    ``bwd_states`` to the forward on these same inputs and it saved the chunk-start states
+    (``return_saved``), so the tensor-core backward skips its recompute sweep."""
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape
@@ -187,6 +190,7 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     a.kernel = {"auto": C.M3_KERNEL_AUTO, "generic": C.M3_KERNEL_GENERIC, "tensorcore": C.M3_KERNEL_TENSORCORE}[kernel]
     ws, need = _workspace(a.dims, dev, workspace)
     a.workspace, a.workspace_bytes = T.ptr(ws), need
+    a.states_ready = 1 if (states_ready and ws is workspace) else 0
     C.check(C.lib().m3_siso_bwd(a, T.stream_handle(dev)))
     return RawGrads(dq=dq, dk=dk, dv=dv, dz=dz, ddt_raw=ddt, da_raw=da, dtrap_raw=dtr, dangles=dang,
                     ddt_bias=ddtb, dq_bias=dqb, dk_bias=dkb, dd_skip=ddsk, dseed_ssm=dss, dseed_k=dsk_,

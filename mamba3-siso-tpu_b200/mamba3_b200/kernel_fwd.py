@@ -112,11 +112,17 @@ def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z
 def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias,
                      d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                      a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
-                     y_out: Optional[torch.Tensor] = None, kernel: str = "auto"):
+                     y_out: Optional[torch.Tensor] = None, kernel: str = "auto",
+                     bwd_states: Optional[torch.Tensor] = None, return_saved: bool = False):
     """Fused boundary: raw ``(B, L, H)`` dt/A/trap streams and head-shared ``(B, L, Nr)``
     angles (all may be strided views of an in_proj output).  Returns
     ``(y, final_ssm, final_k, final_v, final_phi)``.  ``y_out`` may be a strided
-    ``(B, H, L, P)`` view to write into (e.g. a permuted ``(B, L, H, P)`` buffer)."""
+    ``(B, H, L, P)`` view to write into (e.g. a permuted ``(B, L, H, P)`` buffer).
+
+    ``bwd_states``: the workspace of a later `kernel_bwd.siso_backward_raw` on the same
+    inputs; when this forward runs on tensor cores it stores the chunk-start states there
+    and that backward can pass ``states_ready=True``.  ``return_saved`` appends whether it
+    did."""
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v)
     _check_shapes(q, k, v, z)
@@ -159,5 +165,11 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     a.y, a.y_st = T.ptr(y), T.st_bhlp(y)
     a.final_ssm, a.final_k, a.final_v, a.final_phi = T.ptr(fs), T.ptr(fk), T.ptr(fv), T.ptr(fphi)
     a.kernel = _kernel_code(kernel)
+    saved = False
+    if bwd_states is not None and C.lib().m3_siso_fwd_saves_states(a):
+        a.bwd_states, a.bwd_states_bytes = T.ptr(bwd_states), bwd_states.numel() * bwd_states.element_size()
+        saved = True
     C.check(C.lib().m3_siso_fwd(a, T.stream_handle(dev)))
+    if return_saved:
+        return (y, fs, fk, fv, fphi), saved
     return y, fs, fk, fv, fphi

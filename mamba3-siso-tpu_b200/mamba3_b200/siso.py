@@ -83,13 +83,21 @@ class _SegmentFn(torch.autograd.Function):
         if y_blhp:  # write y straight into a (B, L, H, P) buffer, seen as (B, H, L, P)
             b_, l_, h_, p_ = v.shape[0], v.shape[2], v.shape[1], v.shape[3]
             y_out = torch.empty(b_, l_, h_, p_, dtype=v.dtype, device=v.device).permute(0, 2, 1, 3)
-        y, fs, fk, fv, fphi = KF.siso_forward_raw(
+        # with gradients ahead, the backward's workspace is handed to the forward, which fills
+        # in the chunk-start states when it runs on tensor cores (no recompute sweep later)
+        ws = None
+        if any(ctx.needs_input_grad):
+            b_, l_, n_ = q.shape
+            ws = torch.empty(KB.workspace_bytes(b_, l_, v.shape[1], n_, v.shape[3], angles.shape[-1], chunk),
+                             dtype=torch.uint8, device=q.device)
+        (y, fs, fk, fv, fphi), saved = KF.siso_forward_raw(
             q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
             seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, a_floor=a_floor,
-            chunk=chunk, dtype_policy=policy_name, y_out=y_out)
+            chunk=chunk, dtype_policy=policy_name, y_out=y_out, bwd_states=ws, return_saved=True)
         ctx.save_for_backward(q, k, v, z, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip,
                               seed_ssm, seed_k, seed_v, seed_phi)
         ctx.meta = (a_floor, chunk, policy_name)
+        ctx.ws, ctx.saved = ws, saved
         return y, fs, fk, fv, fphi
 
     @staticmethod
@@ -103,7 +111,8 @@ class _SegmentFn(torch.autograd.Function):
             dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
             seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, dfinal_ssm=dfs,
             dfinal_k=dfk, dfinal_v=dfv, dfinal_phi=dfphi, a_floor=a_floor, chunk=chunk,
-            dtype_policy=policy_name)
+            dtype_policy=policy_name, workspace=ctx.ws, states_ready=ctx.saved)
+        ctx.ws = None
 
         def like(x, p):
             return None if (p is None or x is None) else x.to(p.dtype)

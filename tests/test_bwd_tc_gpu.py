@@ -168,3 +168,38 @@ def test_tc_backward_preprocessed_boundary(seeded):
     assert not bad, f"normwise errors vs exact above {BF16_GRAD_TOL}: {bad} (all {errs}; vs generic {vs_gen})"
     bad = {k_: e for k_, e in vs_gen.items() if not e < BF16_GRAD_TOL}
     assert not bad, f"normwise differences vs the generic kernel: {bad}"
+
+
+def test_forward_saved_states_equal_the_recompute_sweep():
+    """The tensor-core forward given the backward's workspace writes the chunk-start states
+    the backward's sweep would recompute: gradients with the sweep skipped equal (bit for
+    bit) those with it; and autograd through `siso_segment` (which uses this) agrees."""
+    from mamba3_b200 import kernel_bwd as KB
+    from mamba3_b200 import kernel_fwd as KF
+    from mamba3_b200 import siso as SISO
+    from mamba3_b200.state import SISOState
+    from tests.gpu_common import dev
+
+    x, st, _ = _raw_case((2, 3, 384, 128, 64, 32, 128), True, seed=45)
+    io = lambda t: dev(t, torch.bfloat16)
+    q, k, v, z, dy = io(x["q"]), io(x["k"]), io(x["v"]), io(x["z"]), io(x["dy"])
+    raw = (dev(x["dt_raw"]), dev(x["a_raw"]), dev(x["trap_raw"]), dev(x["angles"]), dev(x["dt_bias"]),
+           dev(x["q_bias"]), dev(x["k_bias"]))
+    seeds = dict(seed_ssm=dev(st.ssm), seed_k=dev(st.k), seed_v=dev(st.v), seed_phi=dev(st.phi))
+    ws = torch.zeros(KB.workspace_bytes(2, 384, 3, 128, 64, 32, 128), dtype=torch.uint8, device="cuda")
+    _, saved = KF.siso_forward_raw(q, k, v, *raw, d_skip=dev(x["d_skip"]), z=z, **seeds, chunk=128,
+                                   dtype_policy="bf16", bwd_states=ws, return_saved=True)
+    assert saved
+    common = dict(d_skip=dev(x["d_skip"]), z=z, **seeds, chunk=128, dtype_policy="bf16", kernel="tensorcore")
+    g1 = KB.siso_backward_raw(dy, q, k, v, *raw, workspace=ws, states_ready=True, **common)
+    g2 = KB.siso_backward_raw(dy, q, k, v, *raw, **common)
+    for name in ("dq", "dk", "dv", "dz", "ddt_raw", "da_raw", "dtrap_raw", "dangles", "dseed_ssm", "dseed_phi"):
+        a, b = getattr(g1, name), getattr(g2, name)
+        assert torch.allclose(a, b, rtol=1e-6, atol=1e-6), name  # red.add ordering aside, identical
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    out = SISO.siso_segment(*leaves, *raw, d_skip=dev(x["d_skip"]), z=z, state=SISOState(**{
+        "ssm": seeds["seed_ssm"], "k": seeds["seed_k"], "v": seeds["seed_v"], "phi": seeds["seed_phi"]}),
+        chunk=128, policy_name="bf16")
+    out.y.backward(dy)
+    for leaf, ref in zip(leaves, (g2.dq, g2.dk, g2.dv)):
+        assert torch.allclose(leaf.grad.float(), ref.to(torch.bfloat16).float(), rtol=2e-2, atol=1e-3)
