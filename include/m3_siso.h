@@ -91,7 +91,7 @@ typedef struct M3FwdArgs {
   const float *seed_coef;               /* raw == 0: dt_0 (1 - lam_0), (B, H) */
   const float *seed_phi;                /* raw == 1: phi_init (B, H, Nr), may be NULL */
 
-  void *y;            M3Strides y_st;
+  void *y;            M3Strides y_st;   /* NULL: final state only (tensor-core shapes only) */
   float *final_ssm, *final_k, *final_v;
   float *final_phi;                     /* raw == 1: phi at the last position; may be NULL */
 

@@ -201,8 +201,7 @@ int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   if ((rc = check_enums(a.io_dtype, a.policy)) != M3_OK) return rc;
   if ((rc = check_dims(a.dims, 64)) != M3_OK) return rc;
   if ((rc = check_common_inputs(a)) != M3_OK) return rc;
-  if (!a.y || !a.final_ssm || !a.final_k || !a.final_v)
-    return set_error(M3_ERR_ARG, "y, final_ssm, final_k, final_v are required");
+  if (!a.final_ssm || !a.final_k || !a.final_v) return set_error(M3_ERR_ARG, "final_ssm, final_k, final_v are required");
   if (a.chunk_states && a.chunk_states_dtype != M3_DTYPE_F32 && a.chunk_states_dtype != M3_DTYPE_BF16)
     return set_error(M3_ERR_ARG, "chunk_states_dtype must be F32 or BF16");
   fwd_defaults(a);

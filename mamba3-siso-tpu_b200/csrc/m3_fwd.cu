@@ -83,6 +83,12 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
     return set_error(M3_ERR_UNSUPPORTED,
                      "tensor-core forward needs bf16 I/O, bf16 policy, N=128, P=64, chunk % 128 == 0, "
                      "n_angles a multiple of 8 and <= 64, and 16-byte aligned rows");
+  if (!a.y) {  // final state only: the states-only variant of the tensor-core kernel
+    if (!tc_ok || a.kernel == M3_KERNEL_GENERIC)
+      return set_error(M3_ERR_UNSUPPORTED, "y == NULL (final state only) needs the tensor-core forward");
+    const tc::TcStates none{nullptr, nullptr};
+    return run_fwd_tc(a, s, &none);
+  }
   if (tc_ok && a.kernel != M3_KERNEL_GENERIC) {
     if (a.bwd_states) {  // the backward workspace's state region: tiles, then angle carries
       uint8_t* ws = (uint8_t*)a.bwd_states;

@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
     for (int c = 0; c < nchunk && ok; ++c) {
       const int t0 = c * kC;
       const int tg = t0 + t;  // this thread's token (row roles)
-      if (STATES || so.tiles) {  // states-only mode, or a forward saving them for the backward
+      if (so.tiles) {  // the backward's sweep, or a forward saving the states for the backward
         dump_state_tile(c);
         if (RAW && lane == 0 && 8 * lwarp < Nr)
 #pragma unroll
@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_tc_kernel(const M3FwdArgs a, 
       M3_TC_MARK(6);
     }
 
-    if (STATES || so.tiles) {
+    if (so.tiles) {
       slot_sync(slot);
       dump_state_tile(nchunk);
     }

@@ -113,7 +113,8 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
                      d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                      a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
                      y_out: Optional[torch.Tensor] = None, kernel: str = "auto",
-                     bwd_states: Optional[torch.Tensor] = None, return_saved: bool = False):
+                     bwd_states: Optional[torch.Tensor] = None, return_saved: bool = False,
+                     states_only: bool = False):
     """Fused boundary: raw ``(B, L, H)`` dt/A/trap streams and head-shared ``(B, L, Nr)``
     angles (all may be strided views of an in_proj output).  Returns
     ``(y, final_ssm, final_k, final_v, final_phi)``.  ``y_out`` may be a strided
@@ -122,7 +123,8 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     ``bwd_states``: the workspace of a later `kernel_bwd.siso_backward_raw` on the same
     inputs; when this forward runs on tensor cores it stores the chunk-start states there
     and that backward can pass ``states_ready=True``.  ``return_saved`` appends whether it
-    did."""
+    did.  ``states_only``: no y (returned as None), only the final state -- the states-only
+    variant of the tensor-core kernel; see `final_state_supported`."""
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v)
     _check_shapes(q, k, v, z)
@@ -139,7 +141,7 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     dtb, qb, kb, dsk = (T.f32dense(t) for t in (dt_bias, q_bias, k_bias, d_skip))
     s_ssm, s_k, s_v, s_phi = (T.f32dense(t) for t in (seed_ssm, seed_k, seed_v, seed_phi))
     dev = q.device
-    y = y_out if y_out is not None else torch.empty(b, h, l, p, dtype=dt_io, device=dev)
+    y = None if states_only else (y_out if y_out is not None else torch.empty(b, h, l, p, dtype=dt_io, device=dev))
     fs = torch.empty(b, h, p, n, dtype=torch.float32, device=dev)
     fk = torch.empty(b, h, n, dtype=torch.float32, device=dev)
     fv = torch.empty(b, h, p, dtype=torch.float32, device=dev)
@@ -162,7 +164,8 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     a.angles, a.ang_st, a.dt_bias = T.ptr(angles), T.st_bln(angles), T.ptr(dtb)
     a.q_bias, a.k_bias, a.d_skip = T.ptr(qb), T.ptr(kb), T.ptr(dsk)
     a.seed_ssm, a.seed_k, a.seed_v, a.seed_phi = T.ptr(s_ssm), T.ptr(s_k), T.ptr(s_v), T.ptr(s_phi)
-    a.y, a.y_st = T.ptr(y), T.st_bhlp(y)
+    if y is not None:
+        a.y, a.y_st = T.ptr(y), T.st_bhlp(y)
     a.final_ssm, a.final_k, a.final_v, a.final_phi = T.ptr(fs), T.ptr(fk), T.ptr(fv), T.ptr(fphi)
     a.kernel = _kernel_code(kernel)
     saved = False
@@ -173,3 +176,11 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     if return_saved:
         return (y, fs, fk, fv, fphi), saved
     return y, fs, fk, fv, fphi
+
+
+def final_state_supported(q, v, angles, chunk: int, dtype_policy: str = "bf16") -> bool:
+    """Whether `siso_forward_raw(..., states_only=True)` has a kernel for these shapes
+    (the tensor-core ones: bf16 I/O and policy, N = 128, P = 64, chunk % 128 == 0)."""
+    n, p, nr = q.shape[-1], v.shape[-1], angles.shape[-1]
+    return (v.dtype == torch.bfloat16 and T.policy_code(dtype_policy) == C.M3_POLICY_BF16 and n == 128
+            and p == 64 and chunk % 128 == 0 and nr % 8 == 0 and nr <= 64 and q.shape[1] % 128 == 0)

@@ -229,8 +229,9 @@ def siso_segment_seq_parallel(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias,
 
     1. The cumulative angle entering slice r is the carry's phi plus the earlier slices'
        sums of tanh(angle) pi dt (mod 2 pi), from an all-gather of each slice's sum.
-    2. Scan 1 runs the slice from (ssm 0, k 0, v 0, phi_in): its final ssm S_r holds
-       everything the slice itself adds, its final k and v are the true last-token ones.
+    2. Scan 1 runs the slice from (ssm 0, k 0, v 0, phi_in) -- the states-only kernel where
+       the shapes allow, as no y is needed: its final ssm S_r holds everything the slice
+       itself adds, its final k and v are the true last-token ones.
     3. A carry enters a slice as the seeded state S_in + coef v_prev k_prev^T (coef =
        dt_1 (1 - lam_1) of the slice's first token, ``siso.py:207``), which the slice only
        decays, by e^{A} with A the slice's sum of adt.  So after an all-gather of
@@ -281,9 +282,16 @@ def siso_segment_seq_parallel(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias,
     zero = SISOState(ssm=torch.zeros(b, h, p, n, dtype=f32, device=dev), k=torch.zeros(b, h, n, dtype=f32, device=dev),
                      v=torch.zeros(b, h, p, dtype=f32, device=dev), phi=phi_in)
     kw = dict(a_floor=a_floor, chunk=chunk, policy_name=policy_name)
-    first = seg(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z, state=zero, **kw)
+    if segment_fn is None and KF.final_state_supported(q, v, angles, chunk, policy_name):
+        # scan 1 needs no y: the states-only kernel
+        _, fs, fk, fv, fphi = KF.siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias,
+                                                  k_bias, d_skip=d_skip, z=z, seed_ssm=zero.ssm, seed_k=zero.k,
+                                                  seed_v=zero.v, seed_phi=zero.phi, a_floor=a_floor, chunk=chunk,
+                                                  dtype_policy=policy_name, states_only=True)
+        f0 = SISOState(ssm=fs, k=fk, v=fv, phi=fphi)
+    else:
+        f0 = seg(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z, state=zero, **kw).state
     # 3. exchange and rebuild the carry entering this slice
-    f0 = first.state
     parts = gather(torch.cat([f0.ssm.reshape(b, h, -1).double(), f0.k.reshape(b, h, -1).double(),
                               f0.v.reshape(b, h, -1).double(), a_all[..., None], coef[..., None]], dim=-1))
     carry0 = gather(torch.cat([s.reshape(b, h, -1).double() for s in

@@ -84,6 +84,7 @@ def _fwd(**kw):
     (dict(seed_ssm=256), C.M3_ERR_ARG, "together"),
     (dict(io_dtype=7), C.M3_ERR_ARG, "io_dtype"),
     (dict(raw=1), C.M3_ERR_ARG, "raw boundary"),
+    (dict(y=None), C.M3_ERR_UNSUPPORTED, "final state only"),  # f32 I/O has no states-only kernel
 ])
 def test_fwd_validation_errors(mut, code, frag):
     a = _fwd(**mut)
