@@ -64,6 +64,13 @@ def test_filtered_distribution_matches_oracle(vocab, dtype, top_p):
 
 
 @pytest.mark.gpu
+def test_large_vocabulary_uses_the_workspace():
+    """Above 184,320 entries a row's eighth no longer fits in shared memory and the kernel
+    keeps its (key, mass) pairs in the workspace instead."""
+    test_filtered_distribution_matches_oracle(200_003, torch.float32, 0.9)
+
+
+@pytest.mark.gpu
 def test_draws_follow_the_distribution():
     from mamba3_b200.sampling import TokenSampler
 
