@@ -31,8 +31,8 @@ def io_dtype(dt: torch.dtype) -> int:
     raise ValueError(f"unsupported dtype {dt}; want bfloat16 or float32")
 
 
-def policy_code(name: str) -> int:
-    key = name.strip().lower()
+def policy_code(name) -> int:
+    key = str(name).strip().lower()  # a name or a layout.DtypePolicy
     if key in ("bf16", "bfloat16", "default"):
         return C.M3_POLICY_BF16
     if key in ("f32", "fp32", "float32", "highest"):

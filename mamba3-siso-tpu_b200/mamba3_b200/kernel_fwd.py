@@ -83,7 +83,7 @@ def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z
     ybar = states = None
     if save_residuals:
         ybar = torch.empty(b, h, l, p, dtype=torch.float32, device=dev)
-        sdt = torch.bfloat16 if L.policy(dtype_policy) == "bf16" else torch.float32
+        sdt = L.policy(dtype_policy).saved_state
         states = torch.empty(b, h, nc, p, n, dtype=sdt, device=dev)
     a = C.M3FwdArgs()
     a.dims = _dims(q, v, nr, chunk)

@@ -179,3 +179,37 @@ def test_chunked_gradients_vs_finite_differences():
 
     inputs = tuple(x[k].clone().requires_grad_(True) for k in keys)
     assert torch.autograd.gradcheck(f, inputs, eps=1e-6, atol=1e-6, rtol=1e-5)
+
+
+def test_layout_helpers_match_oracle():
+    """The torch rope / prefix-sum helpers of `mamba3_b200.layout` (``layout.py:345-497``)
+    against the oracle's rotation and plain sums; the policy object (``layout.py:243-291``)."""
+    from mamba3_b200 import layout as LA
+
+    g = torch.Generator().manual_seed(3)
+    n, nr = 32, 10
+    phi = torch.rand(2, 5, nr, generator=g, dtype=F64) * 6
+    x = torch.randn(2, 5, n, generator=g, dtype=F64)
+    cos_f, sin_f = LA.rope_cos_sin(phi, n)
+    ocos, osin = O.rope_cos_sin(phi, n)
+    assert torch.allclose(cos_f, ocos) and torch.allclose(sin_f, osin)
+    xr = LA.rope_apply(x, cos_f, sin_f)
+    assert torch.allclose(xr, O.rope_apply(x, ocos, osin))
+    # dphi: derivative of <dx, R(phi) x> in phi, against a finite difference
+    dx = torch.randn(2, 5, n, generator=g, dtype=F64)
+    dphi = LA.rope_dphi(xr, dx, nr)
+    eps = 1e-6
+    for j in (0, 3, nr - 1):
+        pp = phi.clone()
+        pp[..., j] += eps
+        c2, s2 = LA.rope_cos_sin(pp, n)
+        fd = ((LA.rope_apply(x, c2, s2) - xr) * dx).sum(-1) / eps
+        assert torch.allclose(dphi[..., j], fd, atol=1e-4)
+    row = torch.randn(1, 16, generator=g, dtype=F64)
+    tril = LA.tril_ones(16)
+    assert torch.allclose(LA.prefix_sum(row, tril).double(), (row @ tril.double().T)[0], atol=1e-5)
+    assert torch.allclose(LA.suffix_sum(row, tril).double(), (row @ tril.double())[0], atol=1e-5)
+    assert LA.policy("default") is LA.BF16 and LA.policy("highest").highest and LA.policy(LA.F32) is LA.F32
+    assert LA.policy("bf16") == "bf16" and LA.BF16.saved_state == torch.bfloat16
+    with pytest.raises(ValueError):
+        LA.policy("fp8")
