@@ -82,7 +82,8 @@ def _common(a, q, k, v, z, dy, dt_io):
 def siso_backward(dy, q, k, v, adt, gamma, scale, phi, q_bias, k_bias, ybar=None, chunk_states=None,
                   d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_coef=None,
                   dfinal_ssm=None, dfinal_k=None, dfinal_v=None, chunk: int = 128,
-                  dtype_policy: str = "bf16", workspace=None, kernel: str = "auto") -> SISOGrads:
+                  dtype_policy: str = "bf16", workspace=None, kernel: str = "auto", interpret=False,
+                  device_kind=None) -> SISOGrads:
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape

@@ -81,9 +81,10 @@ def _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, raw
 
 
 def siso_decode(q, k, v, adt, dt, lam, angles, q_bias, k_bias, state: SISOState, d_skip=None, z=None,
-                dtype_policy: str = "bf16"):
+                dtype_policy: str = "bf16", interpret=False):
     """One decode step (``kernel_decode.py:252-360``).  ``angles`` are raw (pre-tanh).
-    Returns ``(y, next_state)``; ``y`` is ``(B, H, P)``."""
+    Returns ``(y, next_state)``; ``y`` is ``(B, H, P)``.  ``interpret`` (the reference's
+    Pallas interpret mode) is accepted and has no effect."""
     return _launch(q, k, v, z, angles, q_bias, k_bias, d_skip, state, dtype_policy, False, 0.0,
                    adt=adt, dt=dt, lam=lam)
 
@@ -111,7 +112,7 @@ def decode_step(*args, folded: bool = True, **kw):
 
 
 def decode_loop(q, k, v, adt, dt, lam, angles, q_bias, k_bias, state: SISOState, d_skip=None, z=None,
-                dtype_policy: str = "bf16", folded: bool = False):
+                dtype_policy: str = "bf16", folded: bool = False, interpret=False):
     """``kernel_decode.py:536-573``: one step per token over ``(B, L, ...)`` inputs."""
     outs = []
     for t in range(q.shape[1]):
@@ -123,7 +124,7 @@ def decode_loop(q, k, v, adt, dt, lam, angles, q_bias, k_bias, state: SISOState,
 
 
 def decode_scan(q, k, v, adt, dt, lam, angles, q_bias, k_bias, state: SISOState, d_skip=None, z=None,
-                dtype_policy: str = "bf16", folded: bool = True):
+                dtype_policy: str = "bf16", folded: bool = True, interpret=False):
     """``kernel_decode.py:474-533``: the device-only multi-step driver.  The steps are
     enqueued back to back with no host synchronisation between them; the result is the
     same as `decode_loop`."""

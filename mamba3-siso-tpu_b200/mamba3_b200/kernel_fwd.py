@@ -49,8 +49,11 @@ def _check_shapes(q, k, v, z):
 
 def siso_forward(q, k, v, adt, gamma, scale, phi, q_bias, k_bias, d_skip=None, z=None,
                  seed_ssm=None, seed_k=None, seed_v=None, seed_coef=None, chunk: int = 128,
-                 dtype_policy: str = "bf16", save_residuals: bool = False, out_y=None, kernel: str = "auto"):
-    """Chunked forward at the preprocessed boundary.
+                 dtype_policy: str = "bf16", save_residuals: bool = False, out_y=None, kernel: str = "auto",
+                 interpret=False, device_kind=None):
+    """Chunked forward at the preprocessed boundary.  ``interpret`` / ``device_kind`` are
+    the reference's TPU options (Pallas interpret mode, TPU generation); they are accepted
+    and have no effect here.
 
     Returns ``(y, final_ssm, final_k, final_v)`` and `ForwardResiduals` when
     ``save_residuals`` (``kernel_fwd.py:245-248``).  ``final_k`` is rotated but unscaled.

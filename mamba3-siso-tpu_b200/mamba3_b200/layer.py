@@ -220,8 +220,10 @@ def _scalar_streams(proj: torch.Tensor, cfg: SISOConfig):
     return tail[..., :h], tail[..., h:2 * h], tail[..., 2 * h:3 * h], tail[..., 3 * h:]
 
 
-def mamba3_siso_layer(params: SISOParams, u: torch.Tensor, cfg: SISOConfig, state: Optional[SISOState] = None):
-    """``layer.py:201-262``: ``u (B, L, d_model)`` -> ``(out (B, L, d_model), SISOState)``."""
+def mamba3_siso_layer(params: SISOParams, u: torch.Tensor, cfg: SISOConfig, state: Optional[SISOState] = None,
+                      interpret=False, device_kind=None):
+    """``layer.py:201-262``: ``u (B, L, d_model)`` -> ``(out (B, L, d_model), SISOState)``.
+    ``interpret`` / ``device_kind`` (TPU options of the reference) have no effect."""
     bsz, seqlen, _ = u.shape
     proj = torch.matmul(u, params.in_proj.to(u.dtype))
     z, x, b, c, _, _, _, _ = split_in_proj(proj, cfg)

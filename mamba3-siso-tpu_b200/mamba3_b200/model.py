@@ -93,11 +93,13 @@ def init_lm(cfg: LMConfig, key=0, dtype=torch.float32, device="cuda") -> LMParam
     return LMParams(embed=embed, blocks=blocks, final_norm=torch.ones(cfg.d_model, **to), head=head)
 
 
-def lm_forward(params: LMParams, tokens: torch.Tensor, cfg: LMConfig, states: Optional[List[SISOState]] = None,
-               compute_dtype: Optional[torch.dtype] = None, return_hidden: bool = False, logits: str = "all"):
+def lm_forward(params: LMParams, tokens: torch.Tensor, cfg: LMConfig, interpret=False, device_kind=None,
+               states: Optional[List[SISOState]] = None, compute_dtype: Optional[torch.dtype] = None,
+               return_hidden: bool = False, logits: str = "all"):
     """``model.py:194-232``: ``(B, L)`` tokens -> ``(B, L, vocab)`` logits (and the
     per-layer carry when ``states`` is given).  ``logits="last"`` computes the head for
-    the final position only (``(B, vocab)``), ``"none"`` skips it (prefill for decode)."""
+    the final position only (``(B, vocab)``), ``"none"`` skips it (prefill for decode).
+    ``interpret`` / ``device_kind`` keep the reference's argument order; no effect here."""
     x = params.embed[tokens]
     if compute_dtype is not None:
         x = x.to(compute_dtype)
@@ -132,7 +134,7 @@ def zero_states(cfg: LMConfig, batch: int, dtype=torch.float32, device="cuda") -
 
 @torch.no_grad()
 def lm_decode_step(params: LMParams, token: torch.Tensor, states: List[SISOState], cfg: LMConfig,
-                   compute_dtype: Optional[torch.dtype] = None):
+                   interpret=False, compute_dtype: Optional[torch.dtype] = None):
     """``model.py:244-296``: one token per sequence, ``(B,)`` -> ``(B, vocab)`` logits.
     The per-layer states are updated in place by the decode kernel."""
     c = cfg.siso
@@ -195,11 +197,11 @@ class DecodeGraph:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):
-                lm_decode_step(params, self.tok, states, cfg, compute_dtype)
+                lm_decode_step(params, self.tok, states, cfg, compute_dtype=compute_dtype)
         torch.cuda.current_stream(dev).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.logits, _ = lm_decode_step(params, self.tok, states, cfg, compute_dtype)
+            self.logits, _ = lm_decode_step(params, self.tok, states, cfg, compute_dtype=compute_dtype)
         for st, sn in zip(states, snap):
             for t, s0 in zip(st, sn):
                 t.copy_(s0)

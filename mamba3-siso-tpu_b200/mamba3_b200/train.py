@@ -157,14 +157,14 @@ class _GenerateGraph:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):
-                M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+                M.lm_decode_step(params, smp.token, states, cfg, compute_dtype=compute_dtype)
         torch.cuda.current_stream(dev).wait_stream(side)
         for st, sn in zip(states, snap):
             for t, s0 in zip(st, sn):
                 t.copy_(s0)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            logits, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+            logits, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype=compute_dtype)
             smp.pick(logits)
 
     def replay(self):
@@ -175,7 +175,7 @@ class _GenerateGraph:
 def generate(params: M.LMParams, cfg: M.LMConfig, key, prompt_ids, n_tokens: int = 192, temperature: float = 0.9,
              top_p: float = 0.95, rep_penalty: float = 1.15, rep_window: int = 64,
              stop_ids: Optional[Iterable[int]] = None, on_token: Optional[Callable[[int], None]] = None,
-             compute_dtype=None, device_loop: bool = True, sync_every: int = 32) -> List[int]:
+             compute_dtype=None, device_loop: bool = True, sync_every: int = 32, interpret=False) -> List[int]:
     """``train.py:503-582``: prefill the prompt in whole chunks, feed the remainder token
     by token through `model.lm_decode_step`, then sample ``n_tokens`` (fewer if a stop id
     is drawn; it is included, as in the reference).
@@ -212,7 +212,7 @@ def generate(params: M.LMParams, cfg: M.LMConfig, key, prompt_ids, n_tokens: int
         step = _GenerateGraph(params, cfg, states, smp, compute_dtype).replay
     elif n_tokens > 1:
         def step():
-            lg, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype)
+            lg, _ = M.lm_decode_step(params, smp.token, states, cfg, compute_dtype=compute_dtype)
             smp.pick(lg)
     produced, delivered = 1, 0
     while True:
