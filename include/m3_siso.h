@@ -161,6 +161,8 @@ typedef struct M3BwdArgs {
   size_t workspace_bytes;
 
   int32_t kernel;                         /* M3_KERNEL_*: 0 = pick automatically */
+  int32_t grad_dtype;                     /* M3_DTYPE_* of dv and dz (0 = f32; bf16 halves the
+                                             bytes when the primal v / z are bf16) */
   int32_t states_ready;                   /* 1: `workspace` was passed as bwd_states to an
                                              m3_siso_fwd on these inputs that saved them: the
                                              tensor-core backward skips its recompute sweep */

@@ -25,6 +25,14 @@
 
 namespace m3 {
 
+// dv / dz element in the requested gradient dtype (the struct's pointers are float*)
+__device__ __forceinline__ void store_grad(float* base, size_t i, float v, int32_t dtype) {
+  if (dtype == M3_DTYPE_BF16)
+    reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16(v);
+  else
+    base[i] = v;
+}
+
 constexpr int kBwdSub = 32;
 
 template <int N, int P>
@@ -369,7 +377,7 @@ __global__ void __launch_bounds__(kSimtThreads) bwd_simt_kernel(const M3BwdArgs 
           const float dyv = ld(dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)t * a.dy_st.l + p);
           const float zz = ld(z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)t * a.z_st.l + p);
           const float sg = sigmoidf_(zz);
-          a.dz[(bh * L + t) * P + p] = dyv * ybar * sg * (1.f + zz * (1.f - sg));
+          store_grad(a.dz, (bh * L + t) * P + p, dyv * ybar * sg * (1.f + zz * (1.f - sg)), a.grad_dtype);
         }
       }
     }
@@ -495,7 +503,7 @@ __global__ void __launch_bounds__(kSimtThreads) bwd_simt_kernel(const M3BwdArgs 
           const int p = tx + TL::RX * j;
           float o = acc[i][j] + dg[si] * gs[si * (P + 1) + p];
           if (t == L - 1 && a.dfinal_v) o += a.dfinal_v[bh * P + p];
-          a.dv[(bh * L + t) * P + p] = o;
+          store_grad(a.dv, (bh * L + t) * P + p, o, a.grad_dtype);
         }
       }
     }

@@ -223,6 +223,8 @@ int m3_siso_bwd(const M3BwdArgs* args, void* stream) {
   g_err.clear();
   if (!args) return set_error(M3_ERR_ARG, "args is NULL");
   M3BwdArgs a = *args;
+  if (a.grad_dtype != M3_DTYPE_F32 && a.grad_dtype != M3_DTYPE_BF16)
+    return set_error(M3_ERR_ARG, "grad_dtype must be F32 or BF16");
   int rc;
   if ((rc = check_enums(a.io_dtype, a.policy)) != M3_OK) return rc;
   if ((rc = check_dims(a.dims, 32)) != M3_OK) return rc;

@@ -138,10 +138,12 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
                       d_skip=None, z=None, seed_ssm=None, seed_k=None, seed_v=None, seed_phi=None,
                       dfinal_ssm=None, dfinal_k=None, dfinal_v=None, dfinal_phi=None,
                       a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
-                      workspace=None, kernel: str = "auto", states_ready: bool = False) -> RawGrads:
+                      workspace=None, kernel: str = "auto", states_ready: bool = False,
+                      grad_dtype: torch.dtype = torch.float32) -> RawGrads:
     """Gradients of the fused raw boundary.  ``states_ready``: ``workspace`` was given as
     ``bwd_states`` to the forward on these same inputs and it saved the chunk-start states
-    (``return_saved``), so the tensor-core backward skips its recompute sweep."""
+    (``return_saved``), so the tensor-core backward skips its recompute sweep.
+    ``grad_dtype`` (float32 or bfloat16): the dtype of dv and dz."""
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape
@@ -158,8 +160,9 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     dev, f32 = q.device, torch.float32
     dq = torch.empty(b, l, n, dtype=f32, device=dev)
     dk = torch.empty(b, l, n, dtype=f32, device=dev)
-    dv = torch.empty(b, h, l, p, dtype=f32, device=dev)
-    dz = torch.empty(b, h, l, p, dtype=f32, device=dev) if z is not None else None
+    gdt = grad_dtype if grad_dtype in (torch.float32, torch.bfloat16) else torch.float32
+    dv = torch.empty(b, h, l, p, dtype=gdt, device=dev)
+    dz = torch.empty(b, h, l, p, dtype=gdt, device=dev) if z is not None else None
     ddt = torch.empty(b, l, h, dtype=f32, device=dev)
     da = torch.empty_like(ddt)
     dtr = torch.empty_like(ddt)
@@ -192,6 +195,7 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     ws, need = _workspace(a.dims, dev, workspace)
     a.workspace, a.workspace_bytes = T.ptr(ws), need
     a.states_ready = 1 if (states_ready and ws is workspace) else 0
+    a.grad_dtype = T.io_dtype(gdt)
     C.check(C.lib().m3_siso_bwd(a, T.stream_handle(dev)))
     return RawGrads(dq=dq, dk=dk, dv=dv, dz=dz, ddt_raw=ddt, da_raw=da, dtrap_raw=dtr, dangles=dang,
                     ddt_bias=ddtb, dq_bias=dqb, dk_bias=dkb, dd_skip=ddsk, dseed_ssm=dss, dseed_k=dsk_,

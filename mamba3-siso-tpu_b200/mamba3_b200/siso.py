@@ -111,7 +111,8 @@ class _SegmentFn(torch.autograd.Function):
             dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
             seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, dfinal_ssm=dfs,
             dfinal_k=dfk, dfinal_v=dfv, dfinal_phi=dfphi, a_floor=a_floor, chunk=chunk,
-            dtype_policy=policy_name, workspace=ctx.ws, states_ready=ctx.saved)
+            dtype_policy=policy_name, workspace=ctx.ws, states_ready=ctx.saved,
+            grad_dtype=torch.bfloat16 if v.dtype == torch.bfloat16 else torch.float32)
         ctx.ws = None
 
         def like(x, p):

@@ -203,3 +203,22 @@ def test_forward_saved_states_equal_the_recompute_sweep():
     out.y.backward(dy)
     for leaf, ref in zip(leaves, (g2.dq, g2.dk, g2.dv)):
         assert torch.allclose(leaf.grad.float(), ref.to(torch.bfloat16).float(), rtol=2e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("kernel", ["tensorcore", "generic"])
+def test_bf16_gradient_outputs(kernel):
+    """grad_dtype=bf16: dv / dz written as bf16 equal the fp32 outputs rounded to bf16."""
+    from mamba3_b200 import kernel_bwd as KB
+    from tests.gpu_common import dev
+
+    x, _, _ = _raw_case((1, 2, 256, 128, 64, 32, 128), False, seed=53)
+    io = lambda t: dev(t, torch.bfloat16)
+    args = (io(x["dy"]), io(x["q"]), io(x["k"]), io(x["v"]), dev(x["dt_raw"]), dev(x["a_raw"]), dev(x["trap_raw"]),
+            dev(x["angles"]), dev(x["dt_bias"]), dev(x["q_bias"]), dev(x["k_bias"]))
+    kw = dict(d_skip=dev(x["d_skip"]), z=io(x["z"]), chunk=128, dtype_policy="bf16", kernel=kernel)
+    g32 = KB.siso_backward_raw(*args, **kw)
+    g16 = KB.siso_backward_raw(*args, **kw, grad_dtype=torch.bfloat16)
+    assert g16.dv.dtype == torch.bfloat16 and g16.dz.dtype == torch.bfloat16
+    for a, b in ((g16.dv, g32.dv), (g16.dz, g32.dz)):
+        # the same fp32 values rounded once (red.add order aside, dv / dz involve no atomics)
+        assert (a.float() - b.to(torch.bfloat16).float()).abs().max() <= 1e-2 * b.abs().max()
