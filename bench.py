@@ -564,11 +564,15 @@ def run_profile_case(which):
         toks = torch.randint(0, 256, (8, 8193), device="cuda")
         xs, ys = toks[:, :-1].contiguous(), toks[:, 1:].contiguous()
         for i in range(3):
-            if i == 2:
+            if i == 2:  # the backward runs on autograd's own thread: bracket by profiler start/stop
+                torch.cuda.synchronize()
+                torch.cuda.profiler.start()
                 torch.cuda.nvtx.range_push("train_step")
             step(xs, ys)
             if i == 2:
+                torch.cuda.synchronize()
                 torch.cuda.nvtx.range_pop()
+                torch.cuda.profiler.stop()
         torch.cuda.synchronize()
         return 0
     if which == "generate":  # configs[3] model, B = 1: one decode step + sampling, eager, in an NVTX range
