@@ -166,6 +166,9 @@ typedef struct M3BwdArgs {
   int32_t states_ready;                   /* 1: `workspace` was passed as bwd_states to an
                                              m3_siso_fwd on these inputs that saved them: the
                                              tensor-core backward skips its recompute sweep */
+  M3Strides dv_st, dz_st;                 /* element strides of dv / dz over (B, H, L), P
+                                             contiguous (0 = dense (B, H, L, P)); e.g. a
+                                             (B, L, H, P) buffer seen as (B, H, L, P) */
 } M3BwdArgs;
 
 size_t m3_siso_bwd_workspace_size(const M3Dims *dims);

@@ -377,7 +377,8 @@ __global__ void __launch_bounds__(kSimtThreads) bwd_simt_kernel(const M3BwdArgs 
           const float dyv = ld(dy + (size_t)b * a.dy_st.b + (size_t)h * a.dy_st.h + (size_t)t * a.dy_st.l + p);
           const float zz = ld(z + (size_t)b * a.z_st.b + (size_t)h * a.z_st.h + (size_t)t * a.z_st.l + p);
           const float sg = sigmoidf_(zz);
-          store_grad(a.dz, (bh * L + t) * P + p, dyv * ybar * sg * (1.f + zz * (1.f - sg)), a.grad_dtype);
+          store_grad(a.dz, (size_t)b * a.dz_st.b + (size_t)h * a.dz_st.h + (size_t)t * a.dz_st.l + p,
+                     dyv * ybar * sg * (1.f + zz * (1.f - sg)), a.grad_dtype);
         }
       }
     }
@@ -503,7 +504,8 @@ __global__ void __launch_bounds__(kSimtThreads) bwd_simt_kernel(const M3BwdArgs 
           const int p = tx + TL::RX * j;
           float o = acc[i][j] + dg[si] * gs[si * (P + 1) + p];
           if (t == L - 1 && a.dfinal_v) o += a.dfinal_v[bh * P + p];
-          store_grad(a.dv, (bh * L + t) * P + p, o, a.grad_dtype);
+          store_grad(a.dv, (size_t)b * a.dv_st.b + (size_t)h * a.dv_st.h + (size_t)t * a.dv_st.l + p, o,
+                     a.grad_dtype);
         }
       }
     }

@@ -622,25 +622,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the chunk's dv (and dz) rows are one contiguous 32 KB block each: coalesced stores
       const float* dvs = reinterpret_cast<const float*>(sm + kStDv);
       const float* dzs = reinterpret_cast<const float*>(sm + kStDz);
-      const size_t ob = (bh * L + t0) * kP;
       const bool gbf = a.grad_dtype == M3_DTYPE_BF16;
+      const size_t obv = (size_t)b * a.dv_st.b + (size_t)h * a.dv_st.h + (size_t)t0 * a.dv_st.l;
+      const size_t obz = (size_t)b * a.dz_st.b + (size_t)h * a.dz_st.h + (size_t)t0 * a.dz_st.l;
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         const int idx = tid + kThreads * m, row = idx >> 4, g4 = idx & 15;
         const int so = row * 64 + 4 * (g4 ^ (row & 7));
+        const size_t ov = obv + (size_t)row * a.dv_st.l + 4 * g4, oz = obz + (size_t)row * a.dz_st.l + 4 * g4;
         const float4 v4 = *reinterpret_cast<const float4*>(dvs + so);
         float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if (z) z4 = *reinterpret_cast<const float4*>(dzs + so);
         if (gbf) {  // bf16 gradients: 8-byte stores of 4 rounded values
-          uint2* dvb = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dv) + ob);
-          dvb[idx] = make_uint2(umma::pack_bf16x2(v4.x, v4.y), umma::pack_bf16x2(v4.z, v4.w));
-          if (z) {
-            uint2* dzb = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dz) + ob);
-            dzb[idx] = make_uint2(umma::pack_bf16x2(z4.x, z4.y), umma::pack_bf16x2(z4.z, z4.w));
-          }
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dv) + ov) =
+              make_uint2(umma::pack_bf16x2(v4.x, v4.y), umma::pack_bf16x2(v4.z, v4.w));
+          if (z)
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dz) + oz) =
+                make_uint2(umma::pack_bf16x2(z4.x, z4.y), umma::pack_bf16x2(z4.z, z4.w));
         } else {
-          reinterpret_cast<float4*>(a.dv + ob)[idx] = v4;
-          if (z) reinterpret_cast<float4*>(a.dz + ob)[idx] = z4;
+          *reinterpret_cast<float4*>(a.dv + ov) = v4;
+          if (z) *reinterpret_cast<float4*>(a.dz + oz) = z4;
         }
       }
     }

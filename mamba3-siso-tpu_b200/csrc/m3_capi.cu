@@ -252,6 +252,8 @@ int m3_siso_bwd(const M3BwdArgs* args, void* stream) {
   def_bhlp(a.v_st, a.dims);
   def_bhlp(a.z_st, a.dims);
   def_bhlp(a.dy_st, a.dims);
+  def_bhlp(a.dv_st, a.dims);
+  def_bhlp(a.dz_st, a.dims);
   def_blh(a.raw_st, a.dims);
   def_blx(a.ang_st, a.dims, a.dims.n_angles);
   cudaStream_t s = (cudaStream_t)stream;

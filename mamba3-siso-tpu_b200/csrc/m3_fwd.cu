@@ -134,6 +134,8 @@ bool bwd_tc_eligible(const M3BwdArgs& a) {
   };
   if (!rows_ok(a.dy, a.dy_st)) return false;
   if (!al16(a.dq) || !al16(a.dk) || !al16(a.dv) || (a.dz && !al16(a.dz)) || !al16(a.dangles)) return false;
+  for (const M3Strides* st : {&a.dv_st, &a.dz_st})  // 8-byte (bf16) / 16-byte (f32) row pieces
+    if (st->b % 8 || st->h % 8 || st->l % 8) return false;
   return true;
 }
 

@@ -79,7 +79,7 @@ class M3BwdArgs(ctypes.Structure):
         ("dq_bias", _vp), ("dk_bias", _vp), ("dd_skip", _vp),
         ("dseed_ssm", _vp), ("dseed_k", _vp), ("dseed_v", _vp), ("dseed_coef", _vp), ("dseed_phi", _vp),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
-        ("kernel", _i32), ("grad_dtype", _i32), ("states_ready", _i32),
+        ("kernel", _i32), ("grad_dtype", _i32), ("states_ready", _i32), ("dv_st", M3Strides), ("dz_st", M3Strides),
     ]
 
 

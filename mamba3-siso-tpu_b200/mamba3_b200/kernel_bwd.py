@@ -139,11 +139,12 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
                       dfinal_ssm=None, dfinal_k=None, dfinal_v=None, dfinal_phi=None,
                       a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
                       workspace=None, kernel: str = "auto", states_ready: bool = False,
-                      grad_dtype: torch.dtype = torch.float32) -> RawGrads:
+                      grad_dtype: torch.dtype = torch.float32, dv_out=None, dz_out=None) -> RawGrads:
     """Gradients of the fused raw boundary.  ``states_ready``: ``workspace`` was given as
     ``bwd_states`` to the forward on these same inputs and it saved the chunk-start states
     (``return_saved``), so the tensor-core backward skips its recompute sweep.
-    ``grad_dtype`` (float32 or bfloat16): the dtype of dv and dz."""
+    ``grad_dtype`` (float32 or bfloat16): the dtype of dv and dz.  ``dv_out`` / ``dz_out``:
+    ``(B, H, L, P)`` views (P contiguous, e.g. of a ``(B, L, H, P)`` buffer) to write them into."""
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v, dy)
     b, l, n = q.shape
@@ -161,8 +162,11 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     dq = torch.empty(b, l, n, dtype=f32, device=dev)
     dk = torch.empty(b, l, n, dtype=f32, device=dev)
     gdt = grad_dtype if grad_dtype in (torch.float32, torch.bfloat16) else torch.float32
-    dv = torch.empty(b, h, l, p, dtype=gdt, device=dev)
-    dz = torch.empty(b, h, l, p, dtype=gdt, device=dev) if z is not None else None
+    dv = dv_out if dv_out is not None else torch.empty(b, h, l, p, dtype=gdt, device=dev)
+    dz = (dz_out if dz_out is not None else torch.empty(b, h, l, p, dtype=gdt, device=dev)) if z is not None else None
+    for t in (dv, dz):
+        if t is not None and (t.dtype != gdt or t.stride(-1) != 1 or tuple(t.shape) != (b, h, l, p)):
+            raise ValueError("dv_out / dz_out must be (B, H, L, P) views in grad_dtype with P contiguous")
     ddt = torch.empty(b, l, h, dtype=f32, device=dev)
     da = torch.empty_like(ddt)
     dtr = torch.empty_like(ddt)
@@ -196,6 +200,9 @@ def siso_backward_raw(dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_b
     a.workspace, a.workspace_bytes = T.ptr(ws), need
     a.states_ready = 1 if (states_ready and ws is workspace) else 0
     a.grad_dtype = T.io_dtype(gdt)
+    a.dv_st = T.st_bhlp(dv)
+    if dz is not None:
+        a.dz_st = T.st_bhlp(dz)
     C.check(C.lib().m3_siso_bwd(a, T.stream_handle(dev)))
     return RawGrads(dq=dq, dk=dk, dv=dv, dz=dz, ddt_raw=ddt, da_raw=da, dtrap_raw=dtr, dangles=dang,
                     ddt_bias=ddtb, dq_bias=dqb, dk_bias=dkb, dd_skip=ddsk, dseed_ssm=dss, dseed_k=dsk_,

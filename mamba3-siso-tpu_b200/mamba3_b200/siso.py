@@ -107,12 +107,22 @@ class _SegmentFn(torch.autograd.Function):
         a_floor, chunk, policy_name = ctx.meta
         if dy is None:
             dy = torch.zeros(v.shape, dtype=v.dtype, device=v.device)
+        gdt = torch.bfloat16 if v.dtype == torch.bfloat16 else torch.float32
+
+        def out_like(x):  # a gradient buffer with x's layout (e.g. a permuted in_proj slice)
+            if x is None:
+                return None
+            b_, h_, l_, p_ = x.shape
+            if x.stride(3) == 1 and x.stride(1) == p_ and x.stride(2) >= h_ * p_:
+                return torch.empty(b_, l_, h_, p_, dtype=gdt, device=x.device).permute(0, 2, 1, 3)
+            return None
+
         g = KB.siso_backward_raw(
             dy, q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip=d_skip, z=z,
             seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi, dfinal_ssm=dfs,
             dfinal_k=dfk, dfinal_v=dfv, dfinal_phi=dfphi, a_floor=a_floor, chunk=chunk,
             dtype_policy=policy_name, workspace=ctx.ws, states_ready=ctx.saved,
-            grad_dtype=torch.bfloat16 if v.dtype == torch.bfloat16 else torch.float32)
+            grad_dtype=gdt, dv_out=out_like(v), dz_out=out_like(z))
         ctx.ws = None
 
         def like(x, p):
