@@ -210,24 +210,20 @@ class _RMSNormFn(torch.autograd.Function):
         return dx, dw.to(weight.dtype), None
 
 
-def _scalar_streams(proj: torch.Tensor, cfg: SISOConfig):
-    """The dt / A / trap / angle columns as fp32 strided views (one cast, no transposes)."""
-    start = 2 * cfg.d_inner + 2 * cfg.d_state
-    tail = proj[..., start:]
-    if tail.dtype != torch.float32:
-        tail = tail.float()
-    h = cfg.nheads
-    return tail[..., :h], tail[..., h:2 * h], tail[..., 2 * h:3 * h], tail[..., 3 * h:]
-
-
 def mamba3_siso_layer(params: SISOParams, u: torch.Tensor, cfg: SISOConfig, state: Optional[SISOState] = None,
                       interpret=False, device_kind=None):
     """``layer.py:201-262``: ``u (B, L, d_model)`` -> ``(out (B, L, d_model), SISOState)``.
     ``interpret`` / ``device_kind`` (TPU options of the reference) have no effect."""
     bsz, seqlen, _ = u.shape
     proj = torch.matmul(u, params.in_proj.to(u.dtype))
-    z, x, b, c, _, _, _, _ = split_in_proj(proj, cfg)
-    dt_raw, a_raw, trap_raw, angles = _scalar_streams(proj, cfg)
+    # one split of proj (z, x, B, C, the scalar columns), so that autograd assembles the
+    # in_proj gradient with one concatenation instead of zero-filled slices added together
+    h, n = cfg.nheads, cfg.d_state
+    z, x, b, c, tail = torch.split(proj, (cfg.d_inner, cfg.d_inner, n, n, 3 * h + cfg.n_angles), dim=-1)
+    z, x = z.unflatten(-1, (h, cfg.headdim)), x.unflatten(-1, (h, cfg.headdim))
+    if tail.dtype != torch.float32:
+        tail = tail.float()
+    dt_raw, a_raw, trap_raw, angles = tail[..., :h], tail[..., h:2 * h], tail[..., 2 * h:3 * h], tail[..., 3 * h:]
     b = rms_norm(b, params.b_norm_weight, cfg.norm_eps)
     c = rms_norm(c, params.c_norm_weight, cfg.norm_eps)
     out = SISO.siso_segment(
