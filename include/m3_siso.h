@@ -311,6 +311,13 @@ typedef struct M3SampleArgs {
 
 int m3_sample_tokens(const M3SampleArgs *args, void *stream);
 
+/* The gated MLP activation of model.py:125-137 at inference: out (rows, k) = value * silu(gate),
+ * value / gate the two k-wide halves of each x row (bf16; silu(gate) and the product each
+ * rounded to bf16 like the two torch ops it replaces).  k and the row strides multiples of 8,
+ * 16-byte aligned rows. */
+int m3_gated_act_bf16(const void *x, int64_t x_row_stride, void *out, int64_t out_row_stride, int64_t rows,
+                      int32_t k, void *stream);
+
 /* Last error message of this thread ("" if none). */
 const char *m3_last_error(void);
 

@@ -150,6 +150,16 @@ int m3_gemv_bf16(const M3GemvArgs* args, void* stream) {
   return m3::launch_gemv(a, (cudaStream_t)stream);
 }
 
+int m3_gated_act_bf16(const void* x, int64_t x_row_stride, void* out, int64_t out_row_stride, int64_t rows,
+                      int32_t k, void* stream) {
+  if (!x || !out) return m3::set_error(M3_ERR_ARG, "m3_gated_act_bf16: NULL pointer");
+  if (rows < 0 || k <= 0 || k % 8 || x_row_stride % 8 || out_row_stride % 8 || x_row_stride < 2 * (int64_t)k ||
+      out_row_stride < k || ((uintptr_t)x) % 16 || ((uintptr_t)out) % 16)
+    return m3::set_error(M3_ERR_SHAPE, "m3_gated_act_bf16: k and strides must be multiples of 8, rows 16-byte aligned");
+  if (rows == 0) return M3_OK;
+  return m3::launch_gated_act(x, x_row_stride, out, out_row_stride, rows, k, (cudaStream_t)stream);
+}
+
 int m3_sample_tokens(const M3SampleArgs* args, void* stream) {
   if (!args) return m3::set_error(M3_ERR_ARG, "m3_sample_tokens: args is NULL");
   const M3SampleArgs& a = *args;

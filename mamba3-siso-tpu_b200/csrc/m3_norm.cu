@@ -183,4 +183,46 @@ int launch_rms_norm_bwd(const void* x, int64_t xs, const void* w, const float* r
             : run_norm_bwd<float, float>(x, xs, w, rstd, dy, dys, dx, dxs, dw, rows, dim, s);
 }
 
+// ---- gated activation of the MLP (model.py:125-137): out = value * silu(gate) ----------
+// value / gate are the two k-wide halves of each x row; silu(gate) and the product are each
+// rounded to the I/O dtype, as the two torch ops this replaces round them.  8 elements per
+// thread with 16-byte loads when the rows allow it.
+template <typename T>
+__device__ __forceinline__ float rnd_t(float v) {
+  return static_cast<float>(static_cast<T>(v));
+}
+
+template <typename T>
+__global__ void gated_act_kernel(const T* __restrict__ x, int64_t xs, T* __restrict__ out, int64_t os, int64_t rows,
+                                 int k) {
+  const int64_t per_row = k / 8;
+  const int64_t total = rows * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row, c = (i - r * per_row) * 8;
+    const T* row = x + r * xs;
+    T vv[8], gg[8], oo[8];
+    *reinterpret_cast<uint4*>(vv) = *reinterpret_cast<const uint4*>(row + c);
+    *reinterpret_cast<uint4*>(gg) = *reinterpret_cast<const uint4*>(row + k + c);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float g = static_cast<float>(gg[j]);
+      const float sg = rnd_t<T>(g / (1.f + expf(-g)));
+      oo[j] = static_cast<T>(static_cast<float>(vv[j]) * sg);
+    }
+    *reinterpret_cast<uint4*>(out + r * os + c) = *reinterpret_cast<const uint4*>(oo);
+  }
+}
+
+int launch_gated_act(const void* x, int64_t xs, void* out, int64_t os, int64_t rows, int k, cudaStream_t s) {
+  const int64_t total = rows * (k / 8);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total + 255) / 256;
+  const int grid = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  gated_act_kernel<__nv_bfloat16><<<grid > 0 ? grid : 1, 256, 0, s>>>((const __nv_bfloat16*)x, xs, (__nv_bfloat16*)out,
+                                                                      os, rows, k);
+  return check_launch("m3_gated_act");
+}
+
 }  // namespace m3

@@ -120,7 +120,7 @@ class M3GemvArgs(ctypes.Structure):
 EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
            "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
-           "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states")
+           "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states", "m3_gated_act_bf16")
 
 _lib = None
 
@@ -152,6 +152,8 @@ def lib():
         L.m3_device_error.restype = ctypes.c_int
         L.m3_sample_tokens.argtypes = [ctypes.POINTER(M3SampleArgs), _vp]
         L.m3_sample_tokens.restype = ctypes.c_int
+        L.m3_gated_act_bf16.argtypes = [_vp, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _vp]
+        L.m3_gated_act_bf16.restype = ctypes.c_int
         L.m3_gemv_bf16.argtypes = [ctypes.POINTER(M3GemvArgs), _vp]
         L.m3_gemv_bf16.restype = ctypes.c_int
         L.m3_gemv_scratch_floats.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]

@@ -172,8 +172,7 @@ def lm_decode_step(params: LMParams, token: torch.Tensor, states: List[SISOState
                 x = PJ.small_proj(hm, blk.mlp.fc2, silu_gate=True, residual=x)
             else:
                 hm = torch.matmul(LY.rms_norm(x, blk.mlp_norm_gain, c.norm_eps), blk.mlp.fc1.to(x.dtype))
-                value, gate = hm.chunk(2, dim=-1)
-                x = torch.addmm(x, value * F.silu(gate), blk.mlp.fc2.to(x.dtype))
+                x = torch.addmm(x, PJ.gated_act(hm), blk.mlp.fc2.to(x.dtype))
     x = LY.rms_norm(x, params.final_norm, c.norm_eps)
     head = params.embed.t() if cfg.tie_head else params.head
     return torch.matmul(x, head.to(x.dtype)), out_states

@@ -63,3 +63,18 @@ def small_proj(x: torch.Tensor, w: torch.Tensor, *, norm_w: Optional[torch.Tenso
     a.scratch, a.tickets = T.ptr(scratch), T.ptr(tickets)
     C.check(lib.m3_gemv_bf16(a, T.stream_handle(x.device)))
     return out
+
+
+def gated_act(h: torch.Tensor) -> torch.Tensor:
+    """``value * silu(gate)`` of ``h (m, 2k)`` (``model.py:125-137``) in one kernel for bf16
+    rows (``m3_gated_act_bf16``; the same two roundings as the torch ops); the torch ops
+    otherwise."""
+    k = h.shape[-1] // 2
+    if (h.dim() == 2 and h.dtype == torch.bfloat16 and h.is_cuda and h.stride(1) == 1 and k % 8 == 0
+            and h.stride(0) % 8 == 0 and h.data_ptr() % 16 == 0):
+        out = torch.empty(h.shape[0], k, dtype=h.dtype, device=h.device)
+        C.check(C.lib().m3_gated_act_bf16(T.ptr(h), h.stride(0), T.ptr(out), out.stride(0), h.shape[0], k,
+                                          T.stream_handle(h.device)))
+        return out
+    value, gate = h.chunk(2, dim=-1)
+    return value * torch.nn.functional.silu(gate)

@@ -60,3 +60,16 @@ def test_decode_step_small_batch_path(batch, monkeypatch):
         assert _normwise(la.float(), lb.float()) < 2e-2, t
     for a, b in zip(st_a, st_b):  # bf16 rounding differences carried through 6 steps
         assert _normwise(a.ssm, b.ssm) < 2e-2
+
+
+@pytest.mark.parametrize("rows,k", [(256, 4096), (3, 1064)])
+def test_gated_activation_matches_torch(rows, k):
+    """`projection.gated_act` (``m3_gated_act_bf16``) equals value * silu(gate) in torch bf16."""
+    from mamba3_b200 import projection as PJ
+
+    h = torch.randn(rows, 2 * k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(k)).bfloat16()
+    got = PJ.gated_act(h)
+    value, gate = h.chunk(2, dim=-1)
+    want = value * torch.nn.functional.silu(gate)
+    assert got.shape == want.shape and got.dtype == torch.bfloat16
+    assert (got.float() - want.float()).abs().max() <= 1e-2 * want.float().abs().max()
