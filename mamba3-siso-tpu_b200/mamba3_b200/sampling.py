@@ -66,7 +66,10 @@ class TokenSampler:
         if self.history is not None:
             self.history.zero_()
 
-    def _args(self, logits: torch.Tensor, update: bool, probs_out: Optional[torch.Tensor] = None) -> C.M3SampleArgs:
+    def _args(self, logits: torch.Tensor, update: bool, probs_out: Optional[torch.Tensor] = None):
+        """The call's arguments and the logits tensor they point into (a converted copy when
+        the input is not f32 / bf16 with unit column stride): the caller keeps that tensor
+        alive until the call is enqueued, so its memory cannot be handed out before."""
         if logits.dim() != 2 or logits.shape[0] != self.batch or logits.shape[1] < self.vocab:
             raise ValueError(f"logits must be ({self.batch}, >= {self.vocab}), got {tuple(logits.shape)}")
         if logits.dtype not in (torch.float32, torch.bfloat16) or logits.stride(1) != 1:
@@ -87,21 +90,23 @@ class TokenSampler:
                 a.history, a.history_cap = T.ptr(self.history), self.history.shape[1]
         if probs_out is not None:
             a.probs_out, a.probs_ld = T.ptr(probs_out), probs_out.stride(0)
-        return a
+        return a, logits
 
     def pick(self, logits: torch.Tensor) -> torch.Tensor:
         """Draw one id per row from ``(batch, vocab)`` logits and advance the window; the
         result is `token` (a device buffer, updated in place, no host sync)."""
-        a = self._args(logits, update=True)
+        a, keep = self._args(logits, update=True)
         C.check(C.lib().m3_sample_tokens(a, T.stream_handle(self.device)))
+        del keep
         return self.token
 
     def filtered_probs(self, logits: torch.Tensor) -> torch.Tensor:
         """The distribution `pick` draws from (penalty, temperature and nucleus applied),
         without drawing or touching the window."""
         out = torch.empty(self.batch, self.vocab, dtype=torch.float32, device=self.device)
-        a = self._args(logits, update=False, probs_out=out)
+        a, keep = self._args(logits, update=False, probs_out=out)
         sink = torch.empty(self.batch, dtype=torch.int64, device=self.device)
         a.out_token = T.ptr(sink)
         C.check(C.lib().m3_sample_tokens(a, T.stream_handle(self.device)))
+        del keep
         return out

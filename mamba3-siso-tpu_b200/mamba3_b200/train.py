@@ -140,8 +140,9 @@ def _pick_token(logits: torch.Tensor, seen: torch.Tensor, gen, temperature: floa
     smp = TokenSampler(1, vocab, logits.device, seed=_seed_from(gen, logits.device), temperature=temperature,
                        top_p=top_p, rep_penalty=rep_penalty)
     smp.seen.copy_(seen.reshape(1, -1)[:, :vocab].to(torch.int32))
-    a = smp._args(logits.reshape(1, -1), update=False)
+    a, keep = smp._args(logits.reshape(1, -1), update=False)
     C.check(C.lib().m3_sample_tokens(a, T.stream_handle(logits.device)))
+    del keep
     return smp.token[0].clone()
 
 
