@@ -210,12 +210,112 @@ class _RMSNormFn(torch.autograd.Function):
         return dx, dw.to(weight.dtype), None
 
 
+class _MixerFn(torch.autograd.Function):
+    """The layer from the in_proj output to y (``layer.py:226-252``: split, B / C norms,
+    the scan) as one autograd node, so that the backward writes every piece of the in_proj
+    gradient straight into one buffer: dz / dx by the scan's backward through strided
+    outputs, dB / dC by the norm backward's strided dx, the scalar columns by copies.  The
+    forward also hands the scan's backward its workspace (the chunk-start states)."""
+
+    @staticmethod
+    def forward(ctx, proj, bnw, cnw, dt_bias, c_bias, b_bias, d_skip, s_ssm, s_k, s_v, s_phi, cfg):
+        from . import kernel_bwd as KB
+        from . import kernel_fwd as KF
+
+        parts = _mixer_views(proj, cfg)
+        z4, x4, b, c, raws = parts
+        eps = cfg.norm_eps
+        kn, rk = _rms_norm_fused(b, bnw, eps, _row_stride(b, bnw), want_rstd=True)
+        qn, rq = _rms_norm_fused(c, cnw, eps, _row_stride(c, cnw), want_rstd=True)
+        bsz, seqlen = proj.shape[0], proj.shape[1]
+        h, p = cfg.nheads, cfg.headdim
+        ws = torch.empty(KB.workspace_bytes(bsz, seqlen, h, cfg.d_state, p, cfg.n_angles, cfg.chunk),
+                         dtype=torch.uint8, device=proj.device)
+        y_out = torch.empty(bsz, seqlen, h, p, dtype=x4.dtype, device=proj.device).permute(0, 2, 1, 3)
+        (y, fs, fk, fv, fphi), saved = KF.siso_forward_raw(
+            qn, kn, x4, *raws, dt_bias, c_bias, b_bias, d_skip=d_skip, z=z4, seed_ssm=s_ssm, seed_k=s_k, seed_v=s_v,
+            seed_phi=s_phi, a_floor=cfg.a_floor, chunk=cfg.chunk, dtype_policy=cfg.policy_name, y_out=y_out,
+            bwd_states=ws, return_saved=True)
+        ctx.save_for_backward(proj, bnw, cnw, dt_bias, c_bias, b_bias, d_skip, s_ssm, s_k, s_v, s_phi, qn, kn, rq, rk)
+        ctx.cfg, ctx.ws, ctx.saved = cfg, ws, saved
+        return y, fs, fk, fv, fphi
+
+    @staticmethod
+    def backward(ctx, dy, dfs, dfk, dfv, dfphi):
+        from . import _capi as C
+        from . import _tensors as T
+        from . import kernel_bwd as KB
+
+        (proj, bnw, cnw, dt_bias, c_bias, b_bias, d_skip, s_ssm, s_k, s_v, s_phi, qn, kn, rq, rk) = ctx.saved_tensors
+        cfg = ctx.cfg
+        z4, x4, b, c, raws = _mixer_views(proj, cfg)
+        dproj = torch.empty(proj.shape, dtype=proj.dtype, device=proj.device)
+        dz4, dx4, db, dc, draws = _mixer_views(dproj, cfg, convert_tail=False)
+        if dy is None:
+            dy = torch.zeros(x4.shape, dtype=x4.dtype, device=x4.device)
+        g = KB.siso_backward_raw(
+            dy, qn, kn, x4, *raws, dt_bias, c_bias, b_bias, d_skip=d_skip, z=z4, seed_ssm=s_ssm, seed_k=s_k,
+            seed_v=s_v, seed_phi=s_phi, dfinal_ssm=dfs, dfinal_k=dfk, dfinal_v=dfv, dfinal_phi=dfphi,
+            a_floor=cfg.a_floor, chunk=cfg.chunk, dtype_policy=cfg.policy_name, workspace=ctx.ws,
+            states_ready=ctx.saved, grad_dtype=proj.dtype, dv_out=dx4, dz_out=dz4)
+        ctx.ws = None
+        dws = []
+        for x, w, rstd, dn, dx in ((c, cnw, rq, g.dq, dc), (b, bnw, rk, g.dk, db)):
+            dn = dn.to(proj.dtype).contiguous()  # the norm output's gradient in its own dtype
+            dim = x.shape[-1]
+            rows = x.numel() // dim
+            dw = torch.zeros(dim, dtype=torch.float32, device=x.device)
+            C.check(C.lib().m3_rms_norm_bwd(T.ptr(x), _row_stride(x, w), T.ptr(w), T.ptr(rstd), T.ptr(dn), dim,
+                                            T.ptr(dx), _row_stride(dx, w), T.ptr(dw), rows, dim, _dtcode(x), _dtcode(w),
+                                            T.stream_handle(x.device)))
+            dws.append(dw.to(w.dtype))
+        for dst, src in zip(draws, (g.ddt_raw, g.da_raw, g.dtrap_raw, g.dangles)):
+            dst.copy_(src)
+
+        def like(x, ref):
+            return None if (ref is None or x is None) else x.to(ref.dtype)
+
+        return (dproj, dws[1], dws[0], like(g.ddt_bias, dt_bias), like(g.dq_bias, c_bias), like(g.dk_bias, b_bias),
+                like(g.dd_skip, d_skip), like(g.dseed_ssm, s_ssm), like(g.dseed_k, s_k), like(g.dseed_v, s_v),
+                like(g.dseed_phi, s_phi), None)
+
+
+def _mixer_views(proj, cfg, convert_tail=True):
+    """z, x as (B, H, L, P) views, B, C, and the four scalar-column views of one in_proj output."""
+    h, n = cfg.nheads, cfg.d_state
+    z, x, b, c, tail = torch.split(proj, (cfg.d_inner, cfg.d_inner, n, n, 3 * h + cfg.n_angles), dim=-1)
+    z4 = z.unflatten(-1, (h, cfg.headdim)).permute(0, 2, 1, 3)
+    x4 = x.unflatten(-1, (h, cfg.headdim)).permute(0, 2, 1, 3)
+    if convert_tail and tail.dtype != torch.float32:
+        tail = tail.float()
+    return z4, x4, b, c, (tail[..., :h], tail[..., h:2 * h], tail[..., 2 * h:3 * h], tail[..., 3 * h:])
+
+
+def _mixer_fn_ok(proj, params, cfg) -> bool:
+    if not (torch.is_grad_enabled() and proj.is_cuda and proj.dim() == 3 and proj.is_contiguous()):
+        return False
+    if proj.dtype not in (torch.bfloat16, torch.float32) or cfg.d_state > 2048:
+        return False
+    n, d = cfg.d_state, 2 * cfg.d_inner
+    b = proj[..., d:d + n]
+    return _row_stride(b, params.b_norm_weight) is not None and params.b_norm_weight.is_cuda
+
+
 def mamba3_siso_layer(params: SISOParams, u: torch.Tensor, cfg: SISOConfig, state: Optional[SISOState] = None,
                       interpret=False, device_kind=None):
     """``layer.py:201-262``: ``u (B, L, d_model)`` -> ``(out (B, L, d_model), SISOState)``.
     ``interpret`` / ``device_kind`` (TPU options of the reference) have no effect."""
     bsz, seqlen, _ = u.shape
     proj = torch.matmul(u, params.in_proj.to(u.dtype))
+    if _mixer_fn_ok(proj, params, cfg):  # training: one autograd node, one in_proj gradient buffer
+        s = state
+        y, fs, fk, fv, fphi = _MixerFn.apply(
+            proj, params.b_norm_weight, params.c_norm_weight, params.dt_bias, params.c_bias, params.b_bias,
+            params.d_skip, None if s is None else s.ssm, None if s is None else s.k, None if s is None else s.v,
+            None if s is None else s.phi, cfg)
+        y = y.permute(0, 2, 1, 3).reshape(bsz, seqlen, cfg.d_inner)
+        return (torch.matmul(y.to(u.dtype), params.out_proj.to(u.dtype)),
+                SISOState(ssm=fs, k=fk, v=fv, phi=fphi))
     # one split of proj (z, x, B, C, the scalar columns), so that autograd assembles the
     # in_proj gradient with one concatenation instead of zero-filled slices added together
     h, n = cfg.nheads, cfg.d_state
