@@ -183,8 +183,9 @@ int m3_siso_bwd(const M3BwdArgs *args, void *stream);
  * device, resident until exit).  Problems whose m3_siso_bwd_workspace_size() exceeds it
  * fail with M3_ERR_WORKSPACE.  Nothing is allocated.  All calls on a device share the
  * array, so calls that overlap on the GPU race and must be serialised by the caller.
- * The first call on each device resolves the array's address; make it before any stream
- * capture. */
+ * The first call on each device (and the first after its primary context was re-created,
+ * e.g. by cudaDeviceReset) resolves the array's address; make it before any stream
+ * capture.  `stream` must belong to the current device (else M3_ERR_ARG). */
 int m3_siso_bwd_noalloc(const M3BwdArgs *args, void *stream);
 size_t m3_siso_bwd_noalloc_scratch_bytes(void);
 

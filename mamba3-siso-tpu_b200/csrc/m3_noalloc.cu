@@ -21,7 +21,14 @@
 //    cleared between calls (the array keeps the last call's contents);
 //  * the first call on each device resolves the array's device address with
 //    cudaGetSymbolAddress (with that device current); make that first call before any
-//    stream capture begins.
+//    stream capture begins.  The address is cached per device together with the id of
+//    the CUDA context it was resolved in: if the device's primary context is destroyed
+//    and re-created (cudaDeviceReset), the next call resolves it again, so that call
+//    too must come before any capture;
+//  * `stream` must belong to the current device (a stream of another device gets
+//    M3_ERR_ARG: the scratch address is the current device's).
+#include <cuda.h>
+
 #include <mutex>
 
 #include "m3_internal.h"
@@ -35,22 +42,47 @@ static __device__ __align__(256) unsigned char g_scratch[kNoAllocScratchBytes];
 
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of g_scratch on the current device, resolved once per device.  In host
-// code `g_scratch` names a host-side shadow, not device memory, so it is never passed to
-// a kernel directly.
+// Id of the current CUDA context (unique for the life of the process), through the driver
+// entry points the runtime hands out; 0 if they are unavailable.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {  // under g_mu
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess) get_current = (GetCurrent)f;
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess) get_id = (GetId)f;
+    looked_up = true;
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of g_scratch on the current device, resolved once per device and CUDA
+// context.  In host code `g_scratch` names a host-side shadow, not device memory, so it is
+// never passed to a kernel directly.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return m3::set_error(M3_ERR_LAUNCH, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return m3::set_error(M3_ERR_ARG, "device index out of range");
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_scratch_ptr[dev] || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_scratch);
     if (e != cudaSuccess || !p)
       return m3::set_error(M3_ERR_LAUNCH, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = current_context_id();  // the lookup may have created the context
   }
   *out = g_scratch_ptr[dev];
   return M3_OK;
@@ -62,6 +94,18 @@ extern "C" size_t m3_siso_bwd_noalloc_scratch_bytes(void) { return kNoAllocScrat
 
 extern "C" int m3_siso_bwd_noalloc(const M3BwdArgs* args, void* stream) {
   if (!args) return m3::set_error(M3_ERR_ARG, "args is NULL");
+  const M3Dims& d = args->dims;
+  if (d.batch <= 0 || d.seqlen <= 0 || d.nheads <= 0 || d.state_dim <= 0 || d.headdim <= 0 || d.n_angles <= 0 ||
+      d.chunk <= 0)
+    return m3::set_error(M3_ERR_SHAPE, "all dims must be positive");
+  if (stream) {
+    int cur = 0, sdev = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess || cudaStreamGetDevice((cudaStream_t)stream, &sdev) != cudaSuccess)
+      return m3::set_error(M3_ERR_ARG, "m3_siso_bwd_noalloc: cannot query the stream's device");
+    if (sdev != cur)
+      return m3::set_error(M3_ERR_ARG, "m3_siso_bwd_noalloc: the stream belongs to device " + std::to_string(sdev) +
+                                           ", not the current device " + std::to_string(cur));
+  }
   const size_t need = m3_siso_bwd_workspace_size(&args->dims);
   if (need > kNoAllocScratchBytes)
     return m3::set_error(M3_ERR_WORKSPACE,

@@ -43,12 +43,12 @@ def config_from_state_dict(sd: Mapping[str, Any], headdim: int = 64, **overrides
     nheads, d_state = b_bias.shape[0], b_bias.shape[-1]
     d_inner = nheads * headdim
     if d_inner % d_model != 0:
-        raise ValueError(f"nheads*headdim = {d_inner} is not a multiple of d_model = {d_model}; "
-                         f"headdim={headdim} is probably wrong for this checkpoint")
+        raise ValueError(f"inner width {nheads} heads x {headdim} = {d_inner} does not divide evenly by "
+                         f"d_model {d_model}: pass the checkpoint's real headdim")
     cfg = LY.SISOConfig(d_model=d_model, d_state=d_state, headdim=headdim, expand=d_inner // d_model, **overrides)
     if cfg.d_in_proj != d_in_proj:
-        raise ValueError(f"in_proj width {d_in_proj} does not match the config's {cfg.d_in_proj}. This checkpoint "
-                         f"may be MIMO (mimo_rank > 1), which is out of scope, or headdim is not {headdim}.")
+        raise ValueError(f"in_proj has {d_in_proj} output rows; a single-input (SISO) mixer with headdim "
+                         f"{headdim} would have {cfg.d_in_proj}. Multi-input (MIMO) checkpoints are not supported.")
     return cfg
 
 
@@ -63,7 +63,8 @@ def _bias(sd: Mapping[str, Any], prefix: str) -> torch.Tensor:
     arr = _f32(sd[f"{prefix}_bias"])
     if arr.dim() == 3:
         if arr.shape[1] != 1:
-            raise ValueError(f"{prefix}_bias has mimo_rank {arr.shape[1]}; MIMO is out of scope")
+            raise ValueError(f"{prefix}_bias carries {arr.shape[1]} input ranks; only single-input (rank 1) "
+                             f"mixers are supported")
         arr = arr[:, 0]
     return arr
 

@@ -70,8 +70,8 @@ def gated_act(h: torch.Tensor) -> torch.Tensor:
     rows (``m3_gated_act_bf16``; the same two roundings as the torch ops); the torch ops
     otherwise."""
     k = h.shape[-1] // 2
-    if (h.dim() == 2 and h.dtype == torch.bfloat16 and h.is_cuda and h.stride(1) == 1 and k % 8 == 0
-            and h.stride(0) % 8 == 0 and h.data_ptr() % 16 == 0):
+    if (h.dim() == 2 and h.shape[-1] == 2 * k and h.dtype == torch.bfloat16 and h.is_cuda and h.stride(1) == 1
+            and k % 8 == 0 and h.stride(0) % 8 == 0 and h.data_ptr() % 16 == 0):
         out = torch.empty(h.shape[0], k, dtype=h.dtype, device=h.device)
         C.check(C.lib().m3_gated_act_bf16(T.ptr(h), h.stride(0), T.ptr(out), out.stride(0), h.shape[0], k,
                                           T.stream_handle(h.device)))

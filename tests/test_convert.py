@@ -66,7 +66,7 @@ def test_mimo_and_bad_headdim_refused():
     cfg = CV.config_from_state_dict(sd, headdim=16, chunk=64)
     bad = dict(sd)
     bad["B_bias"] = torch.cat([sd["B_bias"], sd["B_bias"]], 1)
-    with pytest.raises(ValueError, match="MIMO"):
+    with pytest.raises(ValueError, match="single-input"):
         CV.torch_to_jax(bad, cfg)
     del bad["B_norm_weight"]
     with pytest.raises(KeyError):

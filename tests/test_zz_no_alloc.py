@@ -5,8 +5,10 @@ it does not own, or a server that forbids device allocation after start-up) get 
 same gradients as from m3_siso_bwd, with the scratch taken from a fixed array inside the
 library instead of a caller-allocated workspace.  This file checks, through the C ABI,
 that two consecutive calls (different inputs, so the second sees the first's leftover
-scratch) each match m3_siso_bwd within the parity tolerance, and that a problem too
-large for the built-in scratch is refused.  It is collected last on purpose.
+scratch) each match m3_siso_bwd within the parity tolerance -- on the generic fp32 kernel
+and on the production bf16 tensor-core kernel, whose scratch holds swizzled chunk-state
+tiles, angle carries and per-sequence buffers -- and that a problem too large for the
+built-in scratch is refused.  It is collected last on purpose.
 """
 
 import ctypes
@@ -87,6 +89,89 @@ def test_noalloc_backward_matches_allocating_entry_point_twice():
         for name in want:
             e = rel_error(got[name], want[name])
             assert e < 1e-5, (seed, name, e)
+
+
+TC = dict(B=2, H=3, L=512, N=128, P=64, NR=32, CHUNK=128)
+
+
+def _tc_case(seed):
+    """bf16 operands (the tensor-core backward's production inputs), fp32 scalars."""
+    c = TC
+    x = make_inputs(c["B"], c["H"], c["L"], state_dim=c["N"], headdim=c["P"], n_angles=c["NR"], seed=seed)
+    x["dt_bias"] = torch.randn(c["H"], dtype=torch.float64, generator=torch.Generator().manual_seed(seed)) * 0.3
+    io = ("q", "k", "v", "z", "dy")
+    return {k: v.to("cuda", torch.bfloat16 if k in io else torch.float32).contiguous() for k, v in x.items()}
+
+
+def _tc_args(C, d):
+    c = TC
+    B_, H_, L_, N_, P_, NR_ = c["B"], c["H"], c["L"], c["N"], c["P"], c["NR"]
+    f = torch.float32
+    e = lambda *s: torch.empty(*s, dtype=f, device="cuda")
+    out = {"dq": e(B_, L_, N_), "dk": e(B_, L_, N_), "dv": e(B_, H_, L_, P_), "dz": e(B_, H_, L_, P_),
+           "ddt_raw": e(B_, L_, H_), "da_raw": e(B_, L_, H_), "dtrap_raw": e(B_, L_, H_),
+           "dangles": e(B_, L_, NR_), "ddt_bias": e(H_), "dq_bias": e(H_, N_), "dk_bias": e(H_, N_),
+           "dd_skip": e(H_)}
+    a = C.M3BwdArgs()
+    a.dims = C.M3Dims(B_, L_, H_, N_, P_, NR_, c["CHUNK"])
+    a.io_dtype, a.policy, a.raw, a.a_floor = C.M3_DTYPE_BF16, C.M3_POLICY_BF16, 1, 1e-4
+    a.kernel = C.M3_KERNEL_TENSORCORE
+    for name in ("q", "k", "v", "z", "dt_raw", "a_raw", "trap_raw", "angles", "dt_bias", "q_bias", "k_bias",
+                 "d_skip", "dy"):
+        setattr(a, name, d[name].data_ptr())
+    for name, t in out.items():
+        setattr(a, name, t.data_ptr())
+    return a, out
+
+
+def test_noalloc_tensor_core_backward_twice():
+    """The production path (bf16 I/O and policy, N = 128, P = 64) out of the static array:
+    two calls in a row with different inputs, each against m3_siso_bwd with a fresh
+    workspace.  dv and dz involve no atomics and must be bit-identical; the head-summed
+    gradients (dq, dk, biases, angles) are accumulated with atomics in a run-dependent
+    order and are compared at the parity tolerance."""
+    C, lib = _lib()
+    a0, _ = _tc_args(C, _tc_case(1))
+    assert lib.m3_siso_bwd_workspace_size(ctypes.byref(a0.dims)) <= lib.m3_siso_bwd_noalloc_scratch_bytes()
+    stream = torch.cuda.current_stream().cuda_stream
+    for seed in (303, 404):
+        d = _tc_case(seed)
+        a, want = _tc_args(C, d)
+        ws = torch.full((lib.m3_siso_bwd_workspace_size(ctypes.byref(a.dims)),), 0x7F, dtype=torch.uint8,
+                        device="cuda")
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        assert lib.m3_siso_bwd(a, stream) == C.M3_OK, lib.m3_last_error()
+        a, got = _tc_args(C, d)
+        assert lib.m3_siso_bwd_noalloc(a, stream) == C.M3_OK, lib.m3_last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(got["dv"], want["dv"]) and torch.equal(got["dz"], want["dz"]), seed
+        for name in want:
+            e = rel_error(got[name], want[name])
+            assert e < 1e-4, (seed, name, e)
+    # and the last call against exact float64 gradients of the same bf16-valued inputs
+    from tests.test_bwd_gpu import BF16_GRAD_TOL, RAW_NAMES, _normwise, _raw_oracle_grads
+
+    c = TC
+    x = make_inputs(c["B"], c["H"], c["L"], state_dim=c["N"], headdim=c["P"], n_angles=c["NR"], seed=404)
+    x["dt_bias"] = torch.randn(c["H"], dtype=torch.float64, generator=torch.Generator().manual_seed(404)) * 0.3
+    r = lambda t: t.to(torch.bfloat16).double()
+    x["dy"] = r(x["dy"])
+    zero = lambda *s: torch.zeros(*s, dtype=torch.float64)
+    cots = (zero(c["B"], c["H"], c["P"], c["N"]), zero(c["B"], c["H"], c["N"]), zero(c["B"], c["H"], c["P"]),
+            zero(c["B"], c["H"], c["NR"]))
+    leaves, _ = _raw_oracle_grads(x, None, cots, c["CHUNK"], policy="f32", cast=r)
+    names = dict(q="dq", k="dk", v="dv", z="dz", dt_raw="ddt_raw", a_raw="da_raw", trap_raw="dtrap_raw",
+                 angles="dangles", dt_bias="ddt_bias", q_bias="dq_bias", k_bias="dk_bias", d_skip="dd_skip")
+    for leaf in RAW_NAMES:
+        e = _normwise(got[names[leaf]], leaves[leaf].grad)
+        assert e < BF16_GRAD_TOL, (leaf, e)
+
+
+def test_noalloc_rejects_bad_dims_before_sizing():
+    C, lib = _lib()
+    a = C.M3BwdArgs()
+    a.dims = C.M3Dims(-4, 8192, -32, 128, 64, 64, 128)  # two negative dims: the size product would wrap
+    assert lib.m3_siso_bwd_noalloc(a, None) == C.M3_ERR_SHAPE
 
 
 def test_noalloc_rejects_problems_beyond_the_scratch():
