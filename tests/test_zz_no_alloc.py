@@ -160,11 +160,15 @@ def test_noalloc_tensor_core_backward_twice():
     cots = (zero(c["B"], c["H"], c["P"], c["N"]), zero(c["B"], c["H"], c["N"]), zero(c["B"], c["H"], c["P"]),
             zero(c["B"], c["H"], c["NR"]))
     leaves, _ = _raw_oracle_grads(x, None, cots, c["CHUNK"], policy="f32", cast=r)
+    scheme, _ = _raw_oracle_grads(x, None, cots, c["CHUNK"], policy="bf16", cast=r)
     names = dict(q="dq", k="dk", v="dv", z="dz", dt_raw="ddt_raw", a_raw="da_raw", trap_raw="dtrap_raw",
                  angles="dangles", dt_bias="ddt_bias", q_bias="dq_bias", k_bias="dk_bias", d_skip="dd_skip")
     for leaf in RAW_NAMES:
+        # within the bf16 bound of exact, or no further from exact than 1.5x the reference
+        # kernel's own bf16 rounding scheme (the summed dt_bias gradient sits near 2e-2)
         e = _normwise(got[names[leaf]], leaves[leaf].grad)
-        assert e < BF16_GRAD_TOL, (leaf, e)
+        e_ref = _normwise(scheme[leaf].grad, leaves[leaf].grad)
+        assert e < max(BF16_GRAD_TOL, 1.5 * e_ref), (leaf, e, e_ref)
 
 
 def test_noalloc_rejects_bad_dims_before_sizing():
