@@ -107,15 +107,26 @@ typedef struct M3FwdArgs {
    * states_ready.  bwd_states_bytes >= m3_siso_bwd_workspace_size(&dims). */
   void *bwd_states;
   size_t bwd_states_bytes;
+
+  /* Optional scratch of m3_siso_fwd_workspace_size(&dims) bytes, 256-byte aligned: the
+   * raw-boundary tensor-core forward stores the head-shared rotary rates tanh(angles) pi
+   * there once instead of computing them once per head.  NULL is allowed (slower). */
+  void *fwd_workspace;
+  size_t fwd_workspace_bytes;
 } M3FwdArgs;
 
 /* Kernel selection for m3_siso_fwd / m3_siso_bwd.  AUTO uses the tcgen05 tensor-core kernel where it
  * applies (bf16 I/O, bf16 policy, N = 128, P = 64, chunk % 128 == 0, n_angles a
  * multiple of 8 and <= 64, 16-byte aligned rows; for the backward also the raw boundary)
  * and the generic CUDA-core kernel otherwise. */
-enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2 };
+enum { M3_KERNEL_AUTO = 0, M3_KERNEL_GENERIC = 1, M3_KERNEL_TENSORCORE = 2, M3_KERNEL_TENSORCORE_V1 = 3 };
+/* M3_KERNEL_TENSORCORE runs the warp-specialised TMA-fed forward where it applies (raw
+ * boundary, y requested, no residual outputs) and the two-sequence tensor-core kernel
+ * otherwise; M3_KERNEL_TENSORCORE_V1 always runs the latter (kept for comparison). */
 
 int m3_siso_fwd(const M3FwdArgs *args, void *stream);
+/* Bytes of M3FwdArgs.fwd_workspace for these dims (B * L * n_angles floats, rounded up). */
+size_t m3_siso_fwd_workspace_size(const M3Dims *dims);
 /* 1 if m3_siso_fwd(args) takes the tensor-core path and so fills bwd_states, else 0. */
 int m3_siso_fwd_saves_states(const M3FwdArgs *args);
 

@@ -215,13 +215,20 @@ int m3_siso_fwd(const M3FwdArgs* args, void* stream) {
   if (a.chunk_states && a.chunk_states_dtype != M3_DTYPE_F32 && a.chunk_states_dtype != M3_DTYPE_BF16)
     return set_error(M3_ERR_ARG, "chunk_states_dtype must be F32 or BF16");
   fwd_defaults(a);
-  if (a.kernel < M3_KERNEL_AUTO || a.kernel > M3_KERNEL_TENSORCORE)
-    return set_error(M3_ERR_ARG, "kernel must be AUTO, GENERIC or TENSORCORE");
+  if (a.kernel < M3_KERNEL_AUTO || a.kernel > M3_KERNEL_TENSORCORE_V1)
+    return set_error(M3_ERR_ARG, "kernel must be AUTO, GENERIC, TENSORCORE or TENSORCORE_V1");
+  if (a.fwd_workspace && ((uintptr_t)a.fwd_workspace) % 256 != 0)
+    return set_error(M3_ERR_ARG, "fwd_workspace must be 256-byte aligned");
   if (a.bwd_states && a.bwd_states_bytes < bwd_workspace_bytes(a.dims))
     return set_error(M3_ERR_WORKSPACE, "bwd_states is smaller than m3_siso_bwd_workspace_size");
   if (a.bwd_states && ((uintptr_t)a.bwd_states) % 256 != 0)
     return set_error(M3_ERR_ARG, "bwd_states must be 256-byte aligned");
   return launch_fwd(a, (cudaStream_t)stream);
+}
+
+size_t m3_siso_fwd_workspace_size(const M3Dims* dims) {
+  if (!dims) return 0;
+  return fwd_workspace_bytes(*dims);
 }
 
 size_t m3_siso_bwd_workspace_size(const M3Dims* dims) {

@@ -2,8 +2,11 @@
 // shape, the generic CUDA-core kernel for everything else.
 #include "m3_fwd_simt.cuh"
 #include "m3_fwd_tc.cuh"
+#include "m3_fwd_ws.cuh"
 #include "m3_bwd_tc.cuh"
 #include "m3_internal.h"
+
+#include <algorithm>
 
 namespace m3 {
 
@@ -74,12 +77,107 @@ int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaSt
   return run_fwd_tc(a, s, &st);
 }
 
+// ---- warp-specialised TMA-fed forward ---------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// bf16 tensor with dims (inner..outer) and element strides of the outer dims; boxes of
+// 64 inner elements x 128 rows (SWIZZLE_128B: one 128-byte row per token).
+static bool make_map(CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims, const int64_t* strides) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  cuuint64_t gd[4], gs[3];
+  cuuint32_t box[4], es[4];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    box[i] = i == 0 ? 64u : i == 1 ? 128u : 1u;
+    es[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gs[i] = (cuuint64_t)strides[i] * 2u;
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), gd, gs, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool fwd_ws_eligible(const M3FwdArgs& a) {
+  if (a.kernel == M3_KERNEL_GENERIC || a.kernel == M3_KERNEL_TENSORCORE_V1) return false;
+  if (!a.raw || !a.y || a.ybar || a.chunk_states) return false;
+  if (!fwd_tc_eligible(a)) return false;
+  return al16(a.q_bias) && al16(a.k_bias);
+}
+
+size_t fwd_workspace_bytes(const M3Dims& d) {
+  return ((size_t)d.batch * d.seqlen * d.n_angles * sizeof(float) + 255) & ~(size_t)255;
+}
+
+static int sm_count() {
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && n[dev]) return n[dev];
+  int c = 148;
+  cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) n[dev] = c;
+  return c;
+}
+
+static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float* phis) {
+  const M3Dims& d = a.dims;
+  CUtensorMap tq, tk, tv, tz, ty;
+  const uint64_t dq[3] = {(uint64_t)d.state_dim, (uint64_t)d.seqlen, (uint64_t)d.batch};
+  const int64_t sq[2] = {a.q_st.l, a.q_st.b}, sk[2] = {a.k_st.l, a.k_st.b};
+  const uint64_t dv[4] = {(uint64_t)d.headdim, (uint64_t)d.seqlen, (uint64_t)d.nheads, (uint64_t)d.batch};
+  const int64_t sv[3] = {a.v_st.l, a.v_st.h, a.v_st.b}, sy[3] = {a.y_st.l, a.y_st.h, a.y_st.b};
+  const int64_t sz[3] = {a.z_st.l, a.z_st.h, a.z_st.b};
+  if (!make_map(&tq, a.q, 3, dq, sq) || !make_map(&tk, a.k, 3, dq, sk) || !make_map(&tv, a.v, 4, dv, sv) ||
+      !make_map(&ty, a.y, 4, dv, sy) || !make_map(&tz, a.z ? a.z : a.v, 4, dv, a.z ? sz : sv))
+    return set_error(M3_ERR_LAUNCH, "m3_siso_fwd: cuTensorMapEncodeTiled failed");
+  const bool pre = a.fwd_workspace && a.fwd_workspace_bytes >= fwd_workspace_bytes(d) &&
+                   ((uintptr_t)a.fwd_workspace % 256) == 0;
+  ws::Extra ex{nullptr, tiles, phis, d.batch * d.nheads};
+  const int nsm = sm_count();
+  if (pre) {
+    float* T = (float*)a.fwd_workspace;
+    const size_t n4 = (size_t)d.batch * d.seqlen * (d.n_angles / 4);
+    const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)nsm * 8);
+    ws::angle_rate_kernel<<<blocks, 256, 0, s>>>(a.angles, a.ang_st, d.batch, d.seqlen, d.n_angles, T);
+    int rc = check_launch("m3_siso_fwd (angle rates)");
+    if (rc != M3_OK) return rc;
+    ex.T = T;
+  }
+  auto* kern = pre ? ws::fwd_ws_kernel<true> : ws::fwd_ws_kernel<false>;
+  static bool attr_done[2][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[pre][dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmemBytes) != cudaSuccess)
+      return check_launch("fwd_ws: cudaFuncSetAttribute");
+    attr_done[pre][dev] = true;
+  }
+  const int grid = std::min(nsm, ex.nunits);
+  kern<<<grid, ws::kThreads, ws::kSmemBytes, s>>>(a, tq, tk, tv, tz, ty, ex);
+  return check_launch("m3_siso_fwd (tensor core, warp-specialised)");
+}
+
 bool fwd_tc_eligible_public(const M3FwdArgs& a) { return fwd_tc_eligible(a); }
 bool fwd_saves_states(const M3FwdArgs& a) { return a.kernel != M3_KERNEL_GENERIC && fwd_tc_eligible(a); }
 
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   const bool tc_ok = fwd_tc_eligible(a);
-  if (a.kernel == M3_KERNEL_TENSORCORE && !tc_ok)
+  if ((a.kernel == M3_KERNEL_TENSORCORE || a.kernel == M3_KERNEL_TENSORCORE_V1) && !tc_ok)
     return set_error(M3_ERR_UNSUPPORTED,
                      "tensor-core forward needs bf16 I/O, bf16 policy, N=128, P=64, chunk % 128 == 0, "
                      "n_angles a multiple of 8 and <= 64, and 16-byte aligned rows");
@@ -90,9 +188,15 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
     return run_fwd_tc(a, s, &none);
   }
   if (tc_ok && a.kernel != M3_KERNEL_GENERIC) {
+    uint8_t* tiles = nullptr;
+    float* phis = nullptr;
     if (a.bwd_states) {  // the backward workspace's state region: tiles, then angle carries
-      uint8_t* ws = (uint8_t*)a.bwd_states;
-      const tc::TcStates save{ws, (float*)(ws + tc_tiles_bytes(a.dims))};
+      tiles = (uint8_t*)a.bwd_states;
+      phis = (float*)(tiles + tc_tiles_bytes(a.dims));
+    }
+    if (fwd_ws_eligible(a)) return run_fwd_ws(a, s, tiles, phis);
+    if (tiles) {
+      const tc::TcStates save{tiles, phis};
       return run_fwd_tc(a, s, nullptr, &save);
     }
     return run_fwd_tc(a, s);

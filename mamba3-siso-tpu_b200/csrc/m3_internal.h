@@ -34,6 +34,7 @@ int launch_bwd_tc(const M3BwdArgs& a, cudaStream_t s);
 int launch_bwd_simt(const M3BwdArgs& a, cudaStream_t s);
 int launch_decode(const M3DecodeArgs& a, cudaStream_t s);
 size_t bwd_workspace_bytes(const M3Dims& d);
+size_t fwd_workspace_bytes(const M3Dims& d);
 int launch_sample(const M3SampleArgs& a, cudaStream_t s);
 int launch_gemv(const M3GemvArgs& a, cudaStream_t s);
 int launch_gated_act(const void* x, int64_t xs, void* out, int64_t os, int64_t rows, int k, cudaStream_t s);

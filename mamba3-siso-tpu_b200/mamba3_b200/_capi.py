@@ -53,12 +53,14 @@ class M3FwdArgs(ctypes.Structure):
         ("final_ssm", _vp), ("final_k", _vp), ("final_v", _vp), ("final_phi", _vp),
         ("ybar", _vp), ("chunk_states", _vp), ("chunk_states_dtype", _i32),
         ("kernel", _i32), ("bwd_states", _vp), ("bwd_states_bytes", ctypes.c_size_t),
+        ("fwd_workspace", _vp), ("fwd_workspace_bytes", ctypes.c_size_t),
     ]
 
 
 M3_KERNEL_AUTO = 0
 M3_KERNEL_GENERIC = 1
 M3_KERNEL_TENSORCORE = 2
+M3_KERNEL_TENSORCORE_V1 = 3
 
 
 class M3BwdArgs(ctypes.Structure):
@@ -117,7 +119,7 @@ class M3GemvArgs(ctypes.Structure):
     ]
 
 
-EXPORTS = ("m3_siso_fwd", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
+EXPORTS = ("m3_siso_fwd", "m3_siso_fwd_workspace_size", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
            "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
            "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states", "m3_gated_act_bf16")
@@ -140,6 +142,8 @@ def lib():
         L.m3_siso_fwd_saves_states.restype = ctypes.c_int
         L.m3_siso_bwd.argtypes = [ctypes.POINTER(M3BwdArgs), _vp]
         L.m3_siso_bwd.restype = ctypes.c_int
+        L.m3_siso_fwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]
+        L.m3_siso_fwd_workspace_size.restype = ctypes.c_size_t
         L.m3_siso_bwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]
         L.m3_siso_bwd_workspace_size.restype = ctypes.c_size_t
         L.m3_siso_decode.argtypes = [ctypes.POINTER(M3DecodeArgs), _vp]
