@@ -17,8 +17,11 @@ in HBM and larger than L2 (nothing is cached between steps).  The same line carr
 * ``cpu_baseline`` -- the CPU oracle restatement of the reference (``oracle/``) timed on
                    this host's cores on a bounded sample of the forward workload.
 
-Multi-GPU (torchrun): weak scaling, each rank runs its own batch of the same shape with
-no collective on the data path (the (b, h) pairs of the scan are independent).
+Multi-GPU (torchrun): strong scaling.  configs[1]'s batch of 8 sequences x 32 heads is
+split over the ranks by batch (B / N per rank, all heads), configs[3]'s decode batch of
+256 likewise, and configs[4]'s global training batch of 64; the (b, h) pairs of the scan
+are independent, so there is no collective on the scan's data path.  ``value`` is the
+global problem's tokens over the slowest rank's device time.
 ``--impl reference`` times the reference's CPU path (the oracle port; JAX is absent, so
 the reference's own Pallas-interpret / reference.py path cannot run) on rank 0.
 """
@@ -236,23 +239,31 @@ def fwd_call(d, c):
 # ----------------------------------------------------------------------------------------
 
 
+def rank_slice(c, world):
+    """This rank's share of configs[1]'s batch (strong scaling: B / world sequences)."""
+    if c["B"] % world:
+        raise SystemExit(f"--gpus {world} does not divide the batch of {c['B']}")
+    return dict(c, B=c["B"] // world)
+
+
 def bench_fwd(c, steps, warmup, world, rank, peaks):
-    d = make_cfg2_inputs(c, seed=1000 + rank)
-    tokens = c["B"] * c["L"]
-    ms = timed(lambda: fwd_call(d, c), steps, warmup, world)
+    cl = rank_slice(c, world)
+    d = make_cfg2_inputs(cl, seed=1000 + rank)
+    tokens = c["B"] * c["L"]  # the global batch
+    ms = timed(lambda: fwd_call(d, cl), steps, warmup, world)
     per_step = ms / steps
-    th = c["B"] * c["L"] * c["H"]
+    th = cl["B"] * cl["L"] * cl["H"]  # one rank's launch
     flops = FWD_FLOP_PER_TOKEN_HEAD * th
     byts = fwd_bytes_per_token_head(c) * th
     return {
-        "tok_s": tokens * world / (per_step / 1e3),
+        "tok_s": tokens / (per_step / 1e3),
         "ms_per_step": per_step,
         "kernel_ms": per_step,
         "flops": flops,
         "bytes": byts,
         "tflops": flops / (per_step / 1e3) / 1e12,
         "gbs": byts / (per_step / 1e3) / 1e9,
-        "launches": steps,
+        "launches": 2 * steps,  # the head-shared rotary-rate pass + the forward kernel
     }, d
 
 
@@ -261,6 +272,8 @@ def bench_e2e(c, steps, warmup, world, rank):
     step (`siso.siso_segment_streamed`)."""
     from mamba3_b200 import siso as S
 
+    glob = c
+    c = rank_slice(c, world)
     d = make_cfg2_inputs(c, seed=2000 + rank)
     names = ["q", "k", "x", "z", "dt_raw", "a_raw", "trap_raw", "angles"]
     host = {n: d[n].cpu().pin_memory() for n in names}
@@ -278,13 +291,15 @@ def bench_e2e(c, steps, warmup, world, rank):
     with torch.no_grad():
         ms = timed(step, steps, warmup, world)
     per = ms / steps
-    return {"value": c["B"] * c["L"] * world / (per / 1e3), "unit": "tok/s", "ms_per_step": per,
+    return {"value": glob["B"] * glob["L"] / (per / 1e3), "unit": "tok/s", "ms_per_step": per,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
 
 def bench_fwd_bwd(c, steps, warmup, world, rank):
     from mamba3_b200 import kernel_bwd as KB
 
+    glob = c
+    c = rank_slice(c, world)
     d = make_cfg2_inputs(c, seed=3000 + rank)
     ws = torch.empty(KB.workspace_bytes(c["B"], c["L"], c["H"], c["N"], c["P"], c["Nr"], c["chunk"]),
                      dtype=torch.uint8, device="cuda")
@@ -308,7 +323,7 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
     per = ms / steps
     th = c["B"] * c["L"] * c["H"]
     flops = (FWD_FLOP_PER_TOKEN_HEAD + BWD_FLOP_PER_TOKEN_HEAD) * th
-    return {"tok_s": c["B"] * c["L"] * world / (per / 1e3), "ms_per_step": per,
+    return {"tok_s": glob["B"] * glob["L"] / (per / 1e3), "ms_per_step": per,
             "tflops": flops / (per / 1e3) / 1e12,
             "launches_per_step": 2 if saved else 3}  # fwd (saving the states) + bwd; else + the recompute sweep
 
@@ -383,9 +398,10 @@ def bench_train(steps, warmup, world, rank, global_batch=64, seq_len=8192):
             "data": "synthetic order-3 Markov bytes, Dirichlet(0.1) rows"}
 
 
-def bench_decode(steps, warmup, world, rank, peaks, batch=256):
+def bench_decode(steps, warmup, world, rank, peaks, global_batch=256):
     """24-layer LM, d_model 2048, N 128, P 64, H 64, Nr 32, MLP 4096,
-    vocab 128256, bf16 weights, B=256 (per rank), state pre-filled by a 512-token prefill."""
+    vocab 128256, bf16 weights, global B=256 split over the ranks, state pre-filled by a
+    512-token prefill.  µs/token = the slowest rank's step time / 256."""
     from mamba3_b200 import kernel_decode as KD
     from mamba3_b200 import layer as LY
     from mamba3_b200 import model as M
@@ -394,6 +410,7 @@ def bench_decode(steps, warmup, world, rank, peaks, batch=256):
                          policy_name="bf16")
     cfg = M.LMConfig(vocab_size=128256, n_layers=24, siso=scfg, d_intermediate=4096)
     params = M.init_lm(cfg, key=0, dtype=torch.bfloat16)
+    batch = global_batch // world
     g = torch.Generator(device="cuda").manual_seed(4000 + rank)
     prompt = torch.randint(0, cfg.vocab_size, (batch, 512), device="cuda", generator=g)
     states = M.zero_states(cfg, batch)
@@ -420,7 +437,7 @@ def bench_decode(steps, warmup, world, rank, peaks, batch=256):
     byts = batch * H * (2 * P * N * 4 + 2 * (N + P) * 4 + 2 * Nr * 4 + 3 * P * 2 + 3 * 4)
     gbs = byts / (kper / 1e3) / 1e9
     gen = bench_generate(params, cfg, rank)
-    return {"us_per_token": per * 1e3 / batch, "ms_per_step": per, "batch_per_gpu": batch,
+    return {"us_per_token": per * 1e3 / global_batch, "ms_per_step": per, "batch_per_gpu": batch,
             "kernel_ms_per_layer": kper, "kernel_gbs": gbs, "kernel_hbm_frac": gbs / peaks["hbm_gbs"],
             "kernel_bytes_per_layer": byts, "launches_per_step": cfg.n_layers, "generate_b1": gen}
 
@@ -535,7 +552,7 @@ def run_reference(args, world, rank):
     v = statistics.median(vals)
     cb["value"] = v
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 65536 / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": 65536 / v * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "configs[1] kernel fwd B8 H32 L8192 N128 P64 chunk128 (CPU sample)",
                        "sample": cb["sample"]},
@@ -707,14 +724,15 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": fwd["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "configs[1]: kernel-level chunked-scan forward, fused raw boundary",
-                   "batch_per_gpu": c["B"], "nheads": c["H"], "seq_len": c["L"], "d_state": c["N"],
+                   "global_batch": c["B"], "batch_per_gpu": c["B"] // world, "nheads": c["H"], "seq_len": c["L"],
+                   "d_state": c["N"],
                    "headdim": c["P"], "n_angles": c["Nr"], "chunk": c["chunk"], "policy": "bf16",
-                   "parallelism": f"bh-sharded x{world} (weak)",
+                   "parallelism": f"bh-sharded x{world} (strong: batch split)",
                    "l2": "inputs larger than L2 (v, z, y are 268 MB each per step)"},
         "roofline": {"bound": "hbm", "achieved": fwd["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": hbm_frac, "traffic": traffic.get(kname),

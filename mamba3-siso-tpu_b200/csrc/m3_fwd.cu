@@ -307,3 +307,14 @@ extern "C" int m3_debug_tc_timing(unsigned long long* out, int reset) {
   return 0;
 }
 #endif
+
+#ifdef M3_WS_TIMING
+extern "C" int m3_debug_ws_timing(unsigned long long* out, int reset) {
+  cudaMemcpyFromSymbol(out, m3::ws::g_ws_wait, sizeof(unsigned long long) * 256);
+  if (reset) {
+    static unsigned long long z[256] = {};
+    cudaMemcpyToSymbol(m3::ws::g_ws_wait, z, sizeof(z));
+  }
+  return 0;
+}
+#endif

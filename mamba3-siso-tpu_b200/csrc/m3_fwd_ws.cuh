@@ -19,13 +19,15 @@
 //               state, so it runs a chunk ahead of the tensor core.
 //   warps 12-15 state and output (thread = TMEM lane): the state pass (bf16 state tile for
 //               the next readout, scaling by the next chunk's exp2(A_last), final state),
-//               the decay mask S -> P (bf16, into the q~ tile, whose MMAs are done), the
+//               the decay mask S -> P (bf16, into TMEM over the S columns just read), the
 //               accumulator seed exp2(A) Yi + (D + gamma u.w) v, the gated output.
 //
 // TMEM (512 columns): S[2] 0..255, Yi[2] 256..383, the fp32 state 384..447 (lane n,
-// column p), the output accumulator 448..511.  Shared memory: two 96 KB stages
-// {q~ 32K, khat 32K, v 16K, vd 16K}, the bf16 state tile 16K; the vd tile of a stage
-// later holds that chunk's z and then its y.
+// column p), the output accumulator 448..511; the bf16 mask P of a chunk is written over
+// the first 64 columns of its S buffer once they are read (the A operand of Ya).  Shared
+// memory: two 96 KB stages {q~ 32K, khat 32K, v 16K, vd 16K}, the bf16 state tile 16K; the
+// vd tile of a stage later holds that chunk's z and then its y.  The q / k rows of a stage
+// are refilled as soon as the chunk's first MMAs are done, its v rows after Ya.
 //
 // The math is kernel_fwd.py:55-201 of the reference with reference.py:104-199's
 // preprocessing fused in; the bf16 rounding points are the reference kernel's
@@ -53,22 +55,30 @@ constexpr uint32_t kOST = 2 * kStageBytes;     // bf16 state tile (B operand of 
 constexpr uint32_t kOSmall = kOST + 16384;
 constexpr uint32_t kTS = 0, kTYi = 256, kTSt = 384, kTAcc = 448;
 constexpr long long kWaitLimit = 4000000000LL;  // SM cycles
+constexpr uint32_t kSuspendNs = 1u << 20;        // try_wait may park the warp this long
 
 struct Small {
-  float dt[2][kC], scl[2][kC], A[2][kC], gam[2][kC];
+  // per-token scalars of three chunks in flight (chunk g in slot g % 3); cf = the decay
+  // from a token to the end of its 32-token block, exp2(A_{block end} - A)
+  float dt[3][kC], scl[3][kC], A[3][kC], gam[3][kC], cf[3][kC];
   float part[2][8][64];  // per rot warp: angle sums of its 16 tokens
   float cbuf[2][64];     // angle carry into the next chunk (written by the last rot warp)
-  uint64_t full_ld[2], rot_done[2], mma1[2], mma2[2], p_ready[2], scal_ready[2], scal_free[2], yfree[2], zfull[2],
-      ystaged[2];
+  // this sequence's biases for rotary pair e (0..3) of group g: [.][e][0][g] = q (lo, lo+1,
+  // hi, hi+1), [.][e][1][g] = the same for k; two copies by sequence parity.  A quarter-warp
+  // (eight groups) reads 128 contiguous bytes.
+  float bias[2][4][2][8][4];
+  uint64_t full_qk[2], full_v[2], rot_done[2], mma1[2], mma2[2], p_ready[2], yfree[2], zfull[2], ystaged[2];
+  uint64_t scal_ready[3], scal_free[3];
   uint64_t state_ready, drain;
   uint32_t tmem;
   int abort_flag;
 };
 constexpr size_t kSmemBytes = kOSmall + sizeof(Small) + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "more shared memory than a B200 CTA can have");
 
 // Arguments beyond M3FwdArgs.
 struct Extra {
-  const float* T;  // tanh(angles) * pi, (B, L, Nr) contiguous; NULL = computed here
+  const float* T;  // tanh(angles) / 2 (turns), (B, L, Nr) contiguous; NULL = computed here
   uint8_t* tiles;  // backward workspace: chunk-start bf16 state tiles (NULL = not saved)
   float* phis;     //                     chunk-start angle carries
   int nunits;
@@ -121,6 +131,26 @@ __device__ __forceinline__ bool rot_any(bool pred) {
   return r != 0;
 }
 
+#ifdef M3_WS_TIMING
+// Diagnostic builds only: cycles spent in each wait site / phase (index = code) and counts.
+__device__ unsigned long long g_ws_wait[2][128];
+#define WS_MARK(code)                                                         \
+  do {                                                                        \
+    if ((threadIdx.x & 31) == 0) {                                            \
+      const long long now_ = clock64();                                       \
+      atomicAdd(&g_ws_wait[0][code], (unsigned long long)(now_ - tmark_));    \
+      atomicAdd(&g_ws_wait[1][code], 1ull);                                   \
+      tmark_ = now_;                                                          \
+    }                                                                         \
+  } while (0)
+#define WS_MARK_INIT long long tmark_ = clock64()
+#else
+#define WS_MARK(code) \
+  do {                \
+  } while (0)
+#define WS_MARK_INIT
+#endif
+
 // Bounded wait on phase `parity` of `mbar`; false on time-out or when another role
 // already gave up (the CTA-wide abort flag).
 __device__ __forceinline__ bool wait(Small* sm, uint64_t* mbar, uint32_t parity, int code) {
@@ -130,11 +160,17 @@ __device__ __forceinline__ bool wait(Small* sm, uint64_t* mbar, uint32_t parity,
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(kSuspendNs)
         : "memory");
+#ifdef M3_WS_TIMING
+    if (done && (threadIdx.x & 31) == 0) {
+      atomicAdd(&g_ws_wait[0][code], (unsigned long long)(clock64() - t0));
+      atomicAdd(&g_ws_wait[1][code], 1ull);
+    }
+#endif
     if (done) return true;
     if (*(volatile int*)&sm->abort_flag) return false;
     if (clock64() - t0 > kWaitLimit) {
@@ -150,6 +186,34 @@ __device__ __forceinline__ bool wait_warp(Small* sm, uint64_t* mbar, uint32_t pa
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) { umma::tmem_ld32(taddr, v); }
+
+// D[tmem] (+)= A[tmem] * B[smem] (kind::f16; A is M = 128 lanes x K packed two bf16 per
+// 32-bit column).  Issued by one thread.
+__device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// x - round_to_nearest(x) for |x| < 2^22, on the FMA pipe (round-to-nearest of the sum
+// with 1.5 * 2^23 leaves the integer part).
+__device__ __forceinline__ float frac_centered(float x) {
+  const float r = (x + 12582912.f) - 12582912.f;
+  return x - r;
+}
 
 __device__ __forceinline__ uint4 tc_pack8(const float* f) {
   return make_uint4(umma::pack_bf16x2(f[0], f[1]), umma::pack_bf16x2(f[2], f[3]), umma::pack_bf16x2(f[4], f[5]),
@@ -183,8 +247,8 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 
-// tanh(angles) * pi, the head-shared rotary rate, into a (B, L, Nr) buffer: computed
-// once per (b, t, r) instead of once per head inside the scan.
+// tanh(angles) / 2, the head-shared rotary rate in turns (pi radians = half a turn), into a
+// (B, L, Nr) buffer: computed once per (b, t, r) instead of once per head inside the scan.
 __global__ void angle_rate_kernel(const float* __restrict__ angles, M3Strides st, int B, int L, int Nr,
                                   float* __restrict__ T) {
   const int q = Nr / 4;
@@ -195,10 +259,10 @@ __global__ void angle_rate_kernel(const float* __restrict__ angles, M3Strides st
     const int t = (int)(bl % L), b = (int)(bl / L);
     const float4 x = *reinterpret_cast<const float4*>(angles + (size_t)b * st.b + (size_t)t * st.l + 4 * r4);
     float4 y;
-    y.x = tanh_acc(x.x) * kPi;
-    y.y = tanh_acc(x.y) * kPi;
-    y.z = tanh_acc(x.z) * kPi;
-    y.w = tanh_acc(x.w) * kPi;
+    y.x = tanh_acc(x.x) * 0.5f;
+    y.y = tanh_acc(x.y) * 0.5f;
+    y.z = tanh_acc(x.z) * 0.5f;
+    y.w = tanh_acc(x.w) * 0.5f;
     *reinterpret_cast<float4*>(T + bl * Nr + 4 * r4) = y;
   }
 }
@@ -217,14 +281,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool saving = ex.tiles != nullptr;
 
   if (threadIdx.x == 0) {
+    for (int s = 0; s < 3; ++s) {
+      umma::mbar_init(&sm->scal_ready[s], 1);
+      umma::mbar_init(&sm->scal_free[s], 12);
+    }
     for (int s = 0; s < 2; ++s) {
-      umma::mbar_init(&sm->full_ld[s], 1);
+      umma::mbar_init(&sm->full_qk[s], 1);
+      umma::mbar_init(&sm->full_v[s], 1);
       umma::mbar_init(&sm->rot_done[s], 8);
       umma::mbar_init(&sm->mma1[s], 1);
       umma::mbar_init(&sm->mma2[s], 1);
       umma::mbar_init(&sm->p_ready[s], 4);
-      umma::mbar_init(&sm->scal_ready[s], 1);
-      umma::mbar_init(&sm->scal_free[s], 12);
       umma::mbar_init(&sm->yfree[s], 1);
       umma::mbar_init(&sm->zfull[s], 1);
       umma::mbar_init(&sm->ystaged[s], 4);
@@ -239,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tm = sm->tmem;
-
+  if (warp < 4) {
   if (warp == 0) {
     // ================================ TMA producer =================================
     if (lane == 0) {
@@ -249,28 +316,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = u / H, h = u % H;
         for (int c = 0; c < nchunk; ++c, ++G) {
           const int s = G & 1;
-          if (G >= 2 && !(ok = wait(sm, &sm->mma2[s], ((G - 2) >> 1) & 1, 21))) break;
           uint8_t* st = base + s * kStageBytes;
-          expect_tx(&sm->full_ld[s], 2 * 32768 + 16384);
           const int t0 = c * kC;
-          tma_load3(st + kOQ, &tq, 0, t0, b, &sm->full_ld[s]);
-          tma_load3(st + kOQ + 16384, &tq, 64, t0, b, &sm->full_ld[s]);
-          tma_load3(st + kOK, &tk, 0, t0, b, &sm->full_ld[s]);
-          tma_load3(st + kOK + 16384, &tk, 64, t0, b, &sm->full_ld[s]);
-          tma_load4(st + kOV, &tv, 0, t0, h, b, &sm->full_ld[s]);
+          // q / k: free once chunk G-2's S, Yi and state update have read them
+          if (G >= 2 && !(ok = wait(sm, &sm->mma1[s], ((G - 2) >> 1) & 1, 21))) break;
+          expect_tx(&sm->full_qk[s], 2 * 32768);
+          tma_load3(st + kOQ, &tq, 0, t0, b, &sm->full_qk[s]);
+          tma_load3(st + kOQ + 16384, &tq, 64, t0, b, &sm->full_qk[s]);
+          tma_load3(st + kOK, &tk, 0, t0, b, &sm->full_qk[s]);
+          tma_load3(st + kOK + 16384, &tk, 64, t0, b, &sm->full_qk[s]);
+          // v: free once chunk G-2's Ya has read it
+          if (G >= 2 && !(ok = wait(sm, &sm->mma2[s], ((G - 2) >> 1) & 1, 22))) break;
+          expect_tx(&sm->full_v[s], 16384);
+          tma_load4(st + kOV, &tv, 0, t0, h, b, &sm->full_v[s]);
         }
       }
       if (!ok) {  // loads in flight land before the CTA exits
-        for (uint32_t g = (G >= 2 ? G - 2 : 0); g < G; ++g) {
-          uint32_t done = 0;
-          const long long t0 = clock64();
-          while (!done && clock64() - t0 < kWaitLimit / 4) {
-            asm volatile(
-                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, p;\n\t}\n"
-                : "=r"(done)
-                : "r"(umma::smem_u32(&sm->full_ld[g & 1])), "r"((g >> 1) & 1)
-                : "memory");
+        for (uint32_t g = (G >= 2 ? G - 2 : 0); g <= G; ++g) {
+          for (int w = 0; w < 2; ++w) {
+            uint32_t done = 0;
+            const long long t0 = clock64();
+            uint64_t* mb = w ? &sm->full_v[g & 1] : &sm->full_qk[g & 1];
+            while (!done && clock64() - t0 < kWaitLimit / 8) {
+              asm volatile(
+                  "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                  "selp.u32 %0, 1, 0, p;\n\t}\n"
+                  : "=r"(done)
+                  : "r"(umma::smem_u32(mb)), "r"((g >> 1) & 1)
+                  : "memory");
+            }
           }
         }
       }
@@ -286,14 +360,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sp = Gp & 1;
         if (!wait(sm, &sm->p_ready[sp], (Gp >> 1) & 1, 31)) return false;
         umma::fence_after_sync();
-        const uint32_t sQ = umma::smem_u32(base + sp * kStageBytes + kOQ);
         const uint32_t sV = umma::smem_u32(base + sp * kStageBytes + kOV);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
-          umma::mma_bf16(tm + kTAcc, umma::smem_desc(sQ + kmaj, 16, 1024), umma::smem_desc(sV + ks * 2048u, 16384, 1024),
-                         id_yi, true);
-        }
+        for (int ks = 0; ks < 8; ++ks)  // A = P from TMEM: 16 bf16 of K per step = 8 columns
+          mma_bf16_tmem_a(tm + kTAcc, tm + kTS + 128 * sp + 8 * ks, umma::smem_desc(sV + ks * 2048u, 16384, 1024),
+                          id_yi, true);
         umma::commit(&sm->mma2[sp]);
         return true;
       };
@@ -370,7 +441,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       load_raw(0);
       for (int c = 0; c < nchunk; ++c, ++G) {
-        const int s = G & 1;
         float dt[4], lam[4], adt[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -402,13 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) A[j] += off;
         if (c + 1 < nchunk) load_raw(c + 1);  // next chunk's raw values in flight
-        if (G >= 2 && !(ok = wait_warp(sm, &sm->scal_free[s], ((G - 2) >> 1) & 1, 41))) break;
-        *reinterpret_cast<float4*>(&sm->dt[s][4 * lane]) = make_float4(dt[0], dt[1], dt[2], dt[3]);
-        *reinterpret_cast<float4*>(&sm->scl[s][4 * lane]) = make_float4(scl[0], scl[1], scl[2], scl[3]);
-        *reinterpret_cast<float4*>(&sm->A[s][4 * lane]) = make_float4(A[0], A[1], A[2], A[3]);
-        *reinterpret_cast<float4*>(&sm->gam[s][4 * lane]) = make_float4(gam[0], gam[1], gam[2], gam[3]);
+        const float Ae = __shfl_sync(0xffffffffu, A[3], lane | 7);  // end of this 32-token block
+        const int s3 = G % 3;
+        if (G >= 3 && !(ok = wait_warp(sm, &sm->scal_free[s3], (G / 3 - 1) & 1, 41))) break;
+        *reinterpret_cast<float4*>(&sm->dt[s3][4 * lane]) = make_float4(dt[0], dt[1], dt[2], dt[3]);
+        *reinterpret_cast<float4*>(&sm->scl[s3][4 * lane]) = make_float4(scl[0], scl[1], scl[2], scl[3]);
+        *reinterpret_cast<float4*>(&sm->A[s3][4 * lane]) = make_float4(A[0], A[1], A[2], A[3]);
+        *reinterpret_cast<float4*>(&sm->gam[s3][4 * lane]) = make_float4(gam[0], gam[1], gam[2], gam[3]);
+        *reinterpret_cast<float4*>(&sm->cf[s3][4 * lane]) =
+            make_float4(ex2(Ae - A[0]), ex2(Ae - A[1]), ex2(Ae - A[2]), ex2(Ae - A[3]));
         __syncwarp();
-        if (lane == 0) arrive(&sm->scal_ready[s]);
+        if (lane == 0) arrive(&sm->scal_ready[s3]);
       }
     }
   } else if (warp == 3) {
@@ -435,7 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       bulk_wait_all();
     }
-  } else if (warp < 12) {
+  }
+  } else {
+  if (warp < 12) {
     // ================================ rotary =========================================
     const int r = warp - 4, p = lane >> 3, g = lane & 7;
     const int tl = 16 * r + 4 * p;  // first of this thread's four tokens in the chunk
@@ -446,51 +522,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < ex.nunits && ok; u += gridDim.x) {
       const int b = u / H, h = u % H;
       const size_t bh = (size_t)u;
-      float qb[16], kb[16];  // this head's biases of the group's 16 state columns (lo 8, hi 8)
+      if (r == 0 && p == 0) {  // this head's biases of group g into shared memory
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float4 q0 = *reinterpret_cast<const float4*>(a.q_bias + h * kN + 64 * e + 8 * g);
-        const float4 q1 = *reinterpret_cast<const float4*>(a.q_bias + h * kN + 64 * e + 8 * g + 4);
-        const float4 k0 = *reinterpret_cast<const float4*>(a.k_bias + h * kN + 64 * e + 8 * g);
-        const float4 k1 = *reinterpret_cast<const float4*>(a.k_bias + h * kN + 64 * e + 8 * g + 4);
-        qb[8 * e + 0] = q0.x; qb[8 * e + 1] = q0.y; qb[8 * e + 2] = q0.z; qb[8 * e + 3] = q0.w;
-        qb[8 * e + 4] = q1.x; qb[8 * e + 5] = q1.y; qb[8 * e + 6] = q1.z; qb[8 * e + 7] = q1.w;
-        kb[8 * e + 0] = k0.x; kb[8 * e + 1] = k0.y; kb[8 * e + 2] = k0.z; kb[8 * e + 3] = k0.w;
-        kb[8 * e + 4] = k1.x; kb[8 * e + 5] = k1.y; kb[8 * e + 6] = k1.z; kb[8 * e + 7] = k1.w;
+        for (int e = 0; e < 4; ++e) {
+          const float* qb = a.q_bias + h * kN + 8 * g + 2 * e;
+          const float* kb = a.k_bias + h * kN + 8 * g + 2 * e;
+          *reinterpret_cast<float4*>(sm->bias[u & 1][e][0][g]) = make_float4(qb[0], qb[1], qb[64], qb[65]);
+          *reinterpret_cast<float4*>(sm->bias[u & 1][e][1][g]) = make_float4(kb[0], kb[1], kb[64], kb[65]);
+        }
       }
-      float carry[8];
+      float carry[8];  // angles are carried in turns
 #pragma unroll
-      for (int e = 0; e < 8; ++e) carry[e] = (grot && a.seed_phi) ? a.seed_phi[bh * Nr + 8 * g + e] : 0.f;
+      for (int e = 0; e < 8; ++e)
+        carry[e] = (grot && a.seed_phi) ? a.seed_phi[bh * Nr + 8 * g + e] * 0.15915494309189535f : 0.f;
+      // rotary rates tanh(angles) / 2 of this thread's 4 tokens x 8 angles of chunk `cc`
+      float th[4][8];
+      auto load_rates = [&](int cc) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (grot) {
+            if constexpr (PRE_T) {
+              ldg8(ex.T + ((size_t)b * L + cc * kC + tl + j) * Nr + 8 * g, th[j]);
+            } else {
+              const float* pa = a.angles + (size_t)b * a.ang_st.b + (size_t)(cc * kC + tl + j) * a.ang_st.l + 8 * g;
+              ld8(pa, ang32, th[j]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) th[j][e] = tanh_acc(th[j][e]) * 0.5f;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) th[j][e] = 0.f;
+          }
+        }
+      };
       bool yok = true;
       for (int c = 0; c < nchunk; ++c, ++G) {
         const int s = G & 1;
         const int t0 = c * kC;
         uint8_t* st = base + s * kStageBytes;
-        bool wok = yok && wait_warp(sm, &sm->scal_ready[s], (G >> 1) & 1, 61) &&
-                   wait_warp(sm, &sm->full_ld[s], (G >> 1) & 1, 62);
-        const float4 dt4 = *reinterpret_cast<const float4*>(&sm->dt[s][tl]);
+        WS_MARK_INIT;
+        load_rates(c);
+        const int s3 = G % 3;
+        bool wok = yok && wait_warp(sm, &sm->scal_ready[s3], (G / 3) & 1, 61);
+        WS_MARK(81);
+        const float4 dt4 = *reinterpret_cast<const float4*>(&sm->dt[s3][tl]);
         const float dtj[4] = {dt4.x, dt4.y, dt4.z, dt4.w};
-        // ---- angle increments, serial prefix over the thread's 4 tokens -------------
+        // ---- angle increments (rates loaded one chunk ahead), serial prefix ----------
         float x[4][8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (grot) {
-            float th[8];
-            if constexpr (PRE_T) {
-              ldg8(ex.T + ((size_t)b * L + t0 + tl + j) * Nr + 8 * g, th);
-            } else {
-              const float* pa = a.angles + (size_t)b * a.ang_st.b + (size_t)(t0 + tl + j) * a.ang_st.l + 8 * g;
-              ld8(pa, ang32, th);
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-              for (int e = 0; e < 8; ++e) th[e] = tanh_acc(th[e]) * kPi;
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[j][e] = th[e] * dtj[j];
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[j][e] = 0.f;
-          }
-        }
+          for (int e = 0; e < 8; ++e) x[j][e] = th[j][e] * dtj[j];
 #pragma unroll
         for (int j = 1; j < 4; ++j)
 #pragma unroll
@@ -512,10 +594,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(&sm->part[s][r][8 * g]) = make_float4(tot[0], tot[1], tot[2], tot[3]);
           *reinterpret_cast<float4*>(&sm->part[s][r][8 * g + 4]) = make_float4(tot[4], tot[5], tot[6], tot[7]);
         }
+        WS_MARK(82);
         if (rot_any(!wok)) {
           ok = false;
           break;
         }
+        WS_MARK(83);
         // ---- carry into this warp's first token --------------------------------------
         float bse[8];
         if (c > 0) {
@@ -527,10 +611,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) bse[e] = carry[e];
         }
-        if (saving && r == 0 && p == 0 && grot) {
+        if (saving && r == 0 && p == 0 && grot) {  // radians in [0, 2 pi), as the backward reads them
           float* dst = ex.phis + (bh * nchunk + c) * Nr + 8 * g;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dst[e] = bse[e];
+          for (int e = 0; e < 8; ++e) dst[e] = (bse[e] - floorf(bse[e])) * kTwoPi;
         }
         for (int rr = 0; rr < r; ++rr) {
           const float4 p0 = *reinterpret_cast<const float4*>(&sm->part[s][rr][8 * g]);
@@ -544,37 +628,54 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float pv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
           float nx[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) nx[e] = wrap_fast(bse[e] + pv[e]);
+          for (int e = 0; e < 8; ++e) {
+            const float t = bse[e] + pv[e];
+            nx[e] = t - floorf(t);  // turns in [0, 1)
+          }
           *reinterpret_cast<float4*>(&sm->cbuf[s][8 * g]) = make_float4(nx[0], nx[1], nx[2], nx[3]);
           *reinterpret_cast<float4*>(&sm->cbuf[s][8 * g + 4]) = make_float4(nx[4], nx[5], nx[6], nx[7]);
           if (c == nchunk - 1 && a.final_phi && grot)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) a.final_phi[bh * Nr + 8 * g + e] = nx[e];
+            for (int e = 0; e < 8; ++e) a.final_phi[bh * Nr + 8 * g + e] = nx[e] * kTwoPi;
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) bse[e] += excl[e];
+        // absolute angles (turns) of the four tokens; the token loop below is rolled to keep
+        // the code small, so it always works on ph[0] and shifts the array by one
+        float ph[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ph[j][e] = bse[e] + x[j][e];
+        WS_MARK(84);
+        wok = wait_warp(sm, &sm->full_qk[s], (G >> 1) & 1, 62);
+        yok = yok && wok;
+        WS_MARK(85);
         // ---- rotation of the four tokens --------------------------------------------
-        const float4 sc4 = *reinterpret_cast<const float4*>(&sm->scl[s][tl]);
+        const float4 sc4 = *reinterpret_cast<const float4*>(&sm->scl[s3][tl]);
         const float sclj[4] = {sc4.x, sc4.y, sc4.z, sc4.w};
         uint8_t* sQ = st + kOQ;
         uint8_t* sK = st + kOK;
-#pragma unroll
+        float sclr = sclj[0];
+#pragma unroll 1
         for (int j = 0; j < 4; ++j) {
           const int t = tl + j;
-          // sin / cos of the wrapped angle, shifted by pi into the SFU's accurate range:
-          // xs = phi mod 2 pi - pi, so (cos phi, sin phi) = -(cos xs, sin xs)
-          float ncs[8], nsn[8];
+          // sin / cos of the angle reduced to [-pi, pi] (the SFU's accurate range)
+          float cs[8], sn[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             if (grot) {
-              const float ph = bse[e] + x[j][e];
-              const float f = ph * 0.15915494309189535f;
-              const float xs = (f - floorf(f)) * kTwoPi - kPi;
-              ncs[e] = cos_approx(xs);  // = -cos(phi)
-              nsn[e] = sin_approx(xs);  // = -sin(phi)
+              const float xs = frac_centered(ph[0][e]) * kTwoPi;
+#ifdef M3_ABL_NO_SFU  // diagnostic ablation: timing only, wrong values
+              cs[e] = 1.f - 0.5f * xs * xs;
+              sn[e] = xs;
+#else
+              cs[e] = cos_approx(xs);
+              sn[e] = sin_approx(xs);
+#endif
             } else {
-              ncs[e] = -1.f;
-              nsn[e] = 0.f;
+              cs[e] = 1.f;
+              sn[e] = 0.f;
             }
           }
           const uint32_t soff = umma::sw128_off(t, g);
@@ -584,23 +685,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint4 ukh = *reinterpret_cast<const uint4*>(sK + 16384 + soff);
           const uint32_t ql[4] = {uql.x, uql.y, uql.z, uql.w}, qh[4] = {uqh.x, uqh.y, uqh.z, uqh.w};
           const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
-          const float2 sc2 = f2s(sclj[j]);
+          const float2 sc2 = f2s(sclr);
+
           const bool fin = a.final_k && c == nchunk - 1 && t == kC - 1;
           uint32_t oq_lo[4], oq_hi[4], ok_lo[4], ok_hi[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            // -cos, -sin of the two pairs 2e, 2e + 1
-            const float2 nc = f2(ncs[2 * e], ncs[2 * e + 1]), ns = f2(nsn[2 * e], nsn[2 * e + 1]);
-            const float2 ulo = add2(bf2f(ql[e]), f2(qb[2 * e], qb[2 * e + 1]));
-            const float2 uhi = add2(bf2f(qh[e]), f2(qb[8 + 2 * e], qb[8 + 2 * e + 1]));
-            const float2 wlo = add2(bf2f(kl[e]), f2(kb[2 * e], kb[2 * e + 1]));
-            const float2 whi = add2(bf2f(kh[e]), f2(kb[8 + 2 * e], kb[8 + 2 * e + 1]));
-            // lo' = lo cos - hi sin = hi (-sin) - lo (-cos);  hi' = lo sin + hi cos
-            const float2 mnc = f2(-nc.x, -nc.y), mns = f2(-ns.x, -ns.y);
-            const float2 qlo = fma2(uhi, ns, mul2(ulo, mnc));
-            const float2 qhi = fma2(ulo, mns, mul2(uhi, mnc));
-            const float2 klo = fma2(whi, ns, mul2(wlo, mnc));
-            const float2 khi = fma2(wlo, mns, mul2(whi, mnc));
+            const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
+            const float4 bq = *reinterpret_cast<const float4*>(sm->bias[u & 1][e][0][g]);
+            const float4 bk = *reinterpret_cast<const float4*>(sm->bias[u & 1][e][1][g]);
+            const float2 ulo = add2(bf2f(ql[e]), f2(bq.x, bq.y));
+            const float2 uhi = add2(bf2f(qh[e]), f2(bq.z, bq.w));
+            const float2 wlo = add2(bf2f(kl[e]), f2(bk.x, bk.y));
+            const float2 whi = add2(bf2f(kh[e]), f2(bk.z, bk.w));
+            // lo' = lo cos - hi sin;  hi' = lo sin + hi cos
+#ifdef M3_ABL_NO_ROT  // diagnostic ablation: timing only, wrong values
+            const float2 qlo = add2(ulo, c2), qhi = add2(uhi, s2), klo = add2(wlo, c2), khi = add2(whi, s2);
+#else
+            const float2 ns2 = f2(-s2.x, -s2.y);
+            const float2 qlo = fma2(uhi, ns2, mul2(ulo, c2));
+            const float2 qhi = fma2(ulo, s2, mul2(uhi, c2));
+            const float2 klo = fma2(whi, ns2, mul2(wlo, c2));
+            const float2 khi = fma2(wlo, s2, mul2(whi, c2));
+#endif
             if (fin) {  // the final k is rotated but unscaled (kernel_fwd.py:192-201)
               float* fk = a.final_k + bh * kN + 8 * g + 2 * e;
               fk[0] = klo.x;
@@ -617,15 +724,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(sQ + 16384 + soff) = make_uint4(oq_hi[0], oq_hi[1], oq_hi[2], oq_hi[3]);
           *reinterpret_cast<uint4*>(sK + soff) = make_uint4(ok_lo[0], ok_lo[1], ok_lo[2], ok_lo[3]);
           *reinterpret_cast<uint4*>(sK + 16384 + soff) = make_uint4(ok_hi[0], ok_hi[1], ok_hi[2], ok_hi[3]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            ph[0][e] = ph[1][e];
+            ph[1][e] = ph[2][e];
+            ph[2][e] = ph[3][e];
+          }
+          sclr = j == 0 ? sclj[1] : j == 1 ? sclj[2] : sclj[3];
         }
+        WS_MARK(86);
         // ---- vd = v exp2(A_last - A) for this warp's 16 rows --------------------------
-        if (G >= 2) yok = wait_warp(sm, &sm->yfree[s], ((G - 2) >> 1) & 1, 63);
+        if (G >= 2) yok = yok && wait_warp(sm, &sm->yfree[s], ((G - 2) >> 1) & 1, 63);
+        yok = yok && wait_warp(sm, &sm->full_v[s], (G >> 1) & 1, 64);
+        WS_MARK(87);
         {
-          const float Alast = sm->A[s][kC - 1];
+          const float Alast = sm->A[s3][kC - 1];
 #pragma unroll
           for (int m = 0; m < 4; ++m) {
             const int idx = lane + 32 * m, row = 16 * r + (idx >> 3), c8 = idx & 7;
-            const float2 e2 = f2s(ex2(Alast - sm->A[s][row]));
+            const float2 e2 = f2s(ex2(Alast - sm->A[s3][row]));
             const uint32_t off = umma::sw128_off(row, c8);
             const uint4 u4 = *reinterpret_cast<const uint4*>(st + kOV + off);
             *reinterpret_cast<uint4*>(st + kOVD + off) =
@@ -637,8 +754,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           arrive(&sm->rot_done[s]);
-          arrive(&sm->scal_free[s]);
+          arrive(&sm->scal_free[s3]);
         }
+        WS_MARK(88);
       }
       if (!ok) break;
     }
@@ -657,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* sST = base + kOST;
       // ---- initial state: seed (+ the trapezoid seed term), scaled for chunk 0 --------
       {
-        if (!(ok = wait_warp(sm, &sm->scal_ready[G0 & 1], (G0 >> 1) & 1, 71))) break;
+        if (!(ok = wait_warp(sm, &sm->scal_ready[G0 % 3], (G0 / 3) & 1, 71))) break;
         float stv[32];
         float coef = 0.f, kprev = 0.f;
         if (a.seed_ssm) {
@@ -665,8 +783,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           coef = softplusf(a.dt_raw[o] + a.dt_bias[h]) * (1.f - sigmoidf_(a.trap_raw[o]));
           kprev = a.seed_k[bh * kN + i];
         }
-        const float eA = exp2f(sm->A[G0 & 1][kC - 1]);
-#pragma unroll
+        const float eA = exp2f(sm->A[G0 % 3][kC - 1]);
+#pragma unroll 1
         for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
@@ -700,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_warp(sm, &sm->mma2[se], (Ge >> 1) & 1, 72)) return false;
         umma::fence_after_sync();
         if (a.z && !wait_warp(sm, &sm->zfull[se], (Ge >> 1) & 1, 73)) return false;
-#pragma unroll
+#pragma unroll 1
         for (int hh = 0; hh < 2; ++hh) {
           float acc[32];
           tmem_ld32(tm + lrow + kTAcc + 32 * hh, acc);
@@ -716,7 +834,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int e = 0; e < 4; ++e) {
                 const float2 zf = bf2f(zw[e]);
                 // silu(z) = z sigmoid(z) = z (0.5 + 0.5 tanh(z / 2))
+#ifdef M3_ABL_NO_SFU
+                const float2 th = mul2(zf, f2s(0.25f));
+#else
                 const float2 th = f2(tanh_approx(0.5f * zf.x), tanh_approx(0.5f * zf.y));
+#endif
                 const float2 sg = fma2(th, f2s(0.5f), f2s(0.5f));
                 w[e] = f2bf(mul2(f2(acc[8 * cc + 2 * e], acc[8 * cc + 2 * e + 1]), mul2(zf, sg)));
               }
@@ -741,16 +863,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < nchunk; ++c, ++G) {
         const int s = G & 1;
         const bool last = c == nchunk - 1;
+        WS_MARK_INIT;
         if (!(ok = wait_warp(sm, &sm->mma1[s], (G >> 1) & 1, 74))) break;
         umma::fence_after_sync();
+        WS_MARK(91);
         // ---- state pass: bf16 tile for the next readout, scale for the next chunk ------
         {
           float eAn = 1.f;
           if (!last) {
-            if (!(ok = wait_warp(sm, &sm->scal_ready[(G + 1) & 1], ((G + 1) >> 1) & 1, 75))) break;
-            eAn = exp2f(sm->A[(G + 1) & 1][kC - 1]);
+            if (!(ok = wait_warp(sm, &sm->scal_ready[(G + 1) % 3], ((G + 1) / 3) & 1, 75))) break;
+            eAn = exp2f(sm->A[(G + 1) % 3][kC - 1]);
           }
-#pragma unroll
+#pragma unroll 1
           for (int hh = 0; hh < 2; ++hh) {
             float stv[32];
             tmem_ld32(tm + lrow + kTSt + 32 * hh, stv);
@@ -791,54 +915,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) arrive(&sm->state_ready);
           }
         }
+        WS_MARK(92);
         // ---- output of the previous chunk ------------------------------------------------
         if (c > 0 && !(ok = epilogue(G - 1, c - 1))) break;
-        // ---- decay mask S -> P (bf16, into this stage's q~ tile), accumulator seed -------
+        WS_MARK(93);
+        // ---- decay mask S -> P (bf16, into TMEM over S's first 64 columns), acc seed ----
         {
-          uint8_t* sQ = base + s * kStageBytes + kOQ;
-          const float* As = sm->A[s];
+          const int s3 = G % 3;
+          const float* As = sm->A[s3];
+          const float* Cf = sm->cf[s3];
           const float Ai = As[i];
+          const uint32_t tS = tm + lrow + kTS + 128 * s;
           float sii = 0.f;
-#pragma unroll
+#pragma unroll 1
           for (int J = 0; J < 4; ++J) {
-            const uint32_t pbase = (J >> 1) * 16384u;
-            if (J > qd) {
+            uint32_t w[16];
+            if (J > qd) {  // above the diagonal block: all zero
 #pragma unroll
-              for (int cc = 0; cc < 4; ++cc)
-                *reinterpret_cast<uint4*>(sQ + pbase + umma::sw128_off(i, 4 * (J & 1) + cc)) = make_uint4(0, 0, 0, 0);
-              continue;
-            }
-            float sv[32];
-            tmem_ld32(tm + lrow + kTS + 128 * s + 32 * J, sv);
-            umma::tmem_wait_ld();
+              for (int e = 0; e < 16; ++e) w[e] = 0u;
+            } else {
+              float sv[32];
+              tmem_ld32(tS + 32 * J, sv);
+              umma::tmem_wait_ld();
+              // off-diagonal blocks: exp2(A_i - A_j) = exp2(A_i - A_end(J)) exp2(A_end(J) - A_j),
+              // both factors <= 1; the diagonal block takes exp2(A_i - A_j) directly
+              const float rf = J < qd ? ex2(Ai - As[32 * J + 31]) : 1.f;
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-              const float4 a0 = *reinterpret_cast<const float4*>(As + 32 * J + 8 * cc);
-              const float4 a1 = *reinterpret_cast<const float4*>(As + 32 * J + 8 * cc + 4);
-              const float aj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-              uint32_t w[4];
+              for (int cc = 0; cc < 4; ++cc) {
+                const float4 a0 = *reinterpret_cast<const float4*>((J < qd ? Cf : As) + 32 * J + 8 * cc);
+                const float4 a1 = *reinterpret_cast<const float4*>((J < qd ? Cf : As) + 32 * J + 8 * cc + 4);
+                const float aj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j0 = 32 * J + 8 * cc + 2 * e;
-                float v0 = sv[8 * cc + 2 * e] * ex2(fminf(Ai - aj[2 * e], 0.f));
-                float v1 = sv[8 * cc + 2 * e + 1] * ex2(fminf(Ai - aj[2 * e + 1], 0.f));
-                if (J == qd) {
-                  if (j0 == i) sii = sv[8 * cc + 2 * e];
-                  if (j0 + 1 == i) sii = sv[8 * cc + 2 * e + 1];
-                  if (j0 >= i) v0 = 0.f;
-                  if (j0 + 1 >= i) v1 = 0.f;
+                for (int e = 0; e < 4; ++e) {
+                  const int j0 = 32 * J + 8 * cc + 2 * e;
+                  float v0, v1;
+                  if (J < qd) {
+                    const float2 t = mul2(mul2(f2(sv[8 * cc + 2 * e], sv[8 * cc + 2 * e + 1]), f2(aj[2 * e], aj[2 * e + 1])),
+                                          f2s(rf));
+                    v0 = t.x;
+                    v1 = t.y;
+                  } else {
+                    v0 = sv[8 * cc + 2 * e] * ex2(fminf(Ai - aj[2 * e], 0.f));
+                    v1 = sv[8 * cc + 2 * e + 1] * ex2(fminf(Ai - aj[2 * e + 1], 0.f));
+                    if (j0 == i) sii = sv[8 * cc + 2 * e];
+                    if (j0 + 1 == i) sii = sv[8 * cc + 2 * e + 1];
+                    if (j0 >= i) v0 = 0.f;
+                    if (j0 + 1 >= i) v1 = 0.f;
+                  }
+                  w[4 * cc + e] = f2bf(f2(v0, v1));
                 }
-                w[e] = f2bf(f2(v0, v1));
               }
-              *reinterpret_cast<uint4*>(sQ + pbase + umma::sw128_off(i, 4 * (J & 1) + cc)) =
-                  make_uint4(w[0], w[1], w[2], w[3]);
             }
+            // P columns 16J .. 16J+15 lie over S columns this thread has already read
+            tmem_st16(tS + 16 * J, w);
           }
-          const float scl = sm->scl[s][i], gam = sm->gam[s][i];
+          const float scl = sm->scl[s3][i], gam = sm->gam[s3][i];
           const float dg = Dh + (scl > 0.f ? gam * sii * rcp_approx(scl) : 0.f);
           const float eA = ex2(Ai);
           const uint8_t* sV = base + s * kStageBytes + kOV;
-#pragma unroll
+#pragma unroll 1
           for (int hh = 0; hh < 2; ++hh) {
             float yi[32];
             tmem_ld32(tm + lrow + kTYi + 64 * s + 32 * hh, yi);
@@ -862,13 +997,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             arrive(&sm->p_ready[s]);
-            arrive(&sm->scal_free[s]);
+            arrive(&sm->scal_free[s3]);
           }
         }
+        WS_MARK(94);
       }
       if (!ok) break;
       if (!(ok = epilogue(G - 1, nchunk - 1))) break;
     }
+  }
   }
 
   umma::fence_before_sync();
