@@ -198,6 +198,22 @@ __device__ __forceinline__ void mma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate));
 }
 
+// 8 consecutive fp32 TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int q = 0; q < 8; ++q) v[q] = __uint_as_float(r[q]);
+}
+// 4 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
 // 16 consecutive 32-bit TMEM columns of this thread's lane (warp-collective).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
@@ -819,35 +835,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma::fence_after_sync();
         if (a.z && !wait_warp(sm, &sm->zfull[se], (Ge >> 1) & 1, 73)) return false;
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          float acc[32];
-          tmem_ld32(tm + lrow + kTAcc + 32 * hh, acc);
-          umma::tmem_wait_ld();
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const uint32_t off = umma::sw128_off(i, 4 * hh + cc);
-            uint32_t w[4];
-            if (a.z) {
-              const uint4 zz = *reinterpret_cast<const uint4*>(vd + off);
-              const uint32_t zw[4] = {zz.x, zz.y, zz.z, zz.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 zf = bf2f(zw[e]);
-                // silu(z) = z sigmoid(z) = z (0.5 + 0.5 tanh(z / 2))
-#ifdef M3_ABL_NO_SFU
-                const float2 th = mul2(zf, f2s(0.25f));
-#else
-                const float2 th = f2(tanh_approx(0.5f * zf.x), tanh_approx(0.5f * zf.y));
-#endif
-                const float2 sg = fma2(th, f2s(0.5f), f2s(0.5f));
-                w[e] = f2bf(mul2(f2(acc[8 * cc + 2 * e], acc[8 * cc + 2 * e + 1]), mul2(zf, sg)));
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) w[e] = f2bf(f2(acc[8 * cc + 2 * e], acc[8 * cc + 2 * e + 1]));
-            }
-            *reinterpret_cast<uint4*>(vd + off) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int cc = 0; cc < 8; ++cc) {  // 8 output columns at a time
+          float acc[8];
+          tmem_ld8(tm + lrow + kTAcc + 8 * cc, acc);
+          const uint32_t off = umma::sw128_off(i, cc);
+          uint32_t zw[4] = {0u, 0u, 0u, 0u};
+          if (a.z) {
+            const uint4 zz = *reinterpret_cast<const uint4*>(vd + off);
+            zw[0] = zz.x; zw[1] = zz.y; zw[2] = zz.z; zw[3] = zz.w;
           }
+          umma::tmem_wait_ld();
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 o = f2(acc[2 * e], acc[2 * e + 1]);
+            if (a.z) {
+              const float2 zf = bf2f(zw[e]);
+              // silu(z) = z sigmoid(z) = z (0.5 + 0.5 tanh(z / 2))
+              const float2 th = f2(tanh_approx(0.5f * zf.x), tanh_approx(0.5f * zf.y));
+              o = mul2(o, mul2(zf, fma2(th, f2s(0.5f), f2s(0.5f))));
+            }
+            w[e] = f2bf(o);
+          }
+          *reinterpret_cast<uint4*>(vd + off) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         umma::fence_async_smem();
         umma::fence_before_sync();
@@ -929,45 +939,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           float sii = 0.f;
 #pragma unroll 1
           for (int J = 0; J < 4; ++J) {
-            uint32_t w[16];
-            if (J > qd) {  // above the diagonal block: all zero
-#pragma unroll
-              for (int e = 0; e < 16; ++e) w[e] = 0u;
-            } else {
-              float sv[32];
-              tmem_ld32(tS + 32 * J, sv);
-              umma::tmem_wait_ld();
-              // off-diagonal blocks: exp2(A_i - A_j) = exp2(A_i - A_end(J)) exp2(A_end(J) - A_j),
-              // both factors <= 1; the diagonal block takes exp2(A_i - A_j) directly
-              const float rf = J < qd ? ex2(Ai - As[32 * J + 31]) : 1.f;
-#pragma unroll
-              for (int cc = 0; cc < 4; ++cc) {
-                const float4 a0 = *reinterpret_cast<const float4*>((J < qd ? Cf : As) + 32 * J + 8 * cc);
-                const float4 a1 = *reinterpret_cast<const float4*>((J < qd ? Cf : As) + 32 * J + 8 * cc + 4);
+            // off-diagonal blocks: exp2(A_i - A_j) = exp2(A_i - A_end(J)) exp2(A_end(J) - A_j),
+            // both factors <= 1; the diagonal block takes exp2(A_i - A_j) directly
+            const float rf = J < qd ? ex2(Ai - As[32 * J + 31]) : 1.f;
+            const float* fac = (J < qd ? Cf : As) + 32 * J;
+#pragma unroll 1
+            for (int cc = 0; cc < 4; ++cc) {  // 8 columns of S -> 4 packed columns of P
+              uint32_t w[4] = {0u, 0u, 0u, 0u};
+              if (J <= qd) {
+                float sv[8];
+                tmem_ld8(tS + 32 * J + 8 * cc, sv);
+                const float4 a0 = *reinterpret_cast<const float4*>(fac + 8 * cc);
+                const float4 a1 = *reinterpret_cast<const float4*>(fac + 8 * cc + 4);
                 const float aj[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                umma::tmem_wait_ld();
+                if (J < qd) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int j0 = 32 * J + 8 * cc + 2 * e;
-                  float v0, v1;
-                  if (J < qd) {
-                    const float2 t = mul2(mul2(f2(sv[8 * cc + 2 * e], sv[8 * cc + 2 * e + 1]), f2(aj[2 * e], aj[2 * e + 1])),
-                                          f2s(rf));
-                    v0 = t.x;
-                    v1 = t.y;
-                  } else {
-                    v0 = sv[8 * cc + 2 * e] * ex2(fminf(Ai - aj[2 * e], 0.f));
-                    v1 = sv[8 * cc + 2 * e + 1] * ex2(fminf(Ai - aj[2 * e + 1], 0.f));
-                    if (j0 == i) sii = sv[8 * cc + 2 * e];
-                    if (j0 + 1 == i) sii = sv[8 * cc + 2 * e + 1];
-                    if (j0 >= i) v0 = 0.f;
-                    if (j0 + 1 >= i) v1 = 0.f;
+                  for (int e = 0; e < 4; ++e)
+                    w[e] = f2bf(mul2(mul2(f2(sv[2 * e], sv[2 * e + 1]), f2(aj[2 * e], aj[2 * e + 1])), f2s(rf)));
+                } else {
+                  const int j0 = 32 * J + 8 * cc;
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) {
+                    if (j0 + e == i) sii = sv[e];
+                    sv[e] = j0 + e < i ? sv[e] * ex2(Ai - aj[e]) : 0.f;
                   }
-                  w[4 * cc + e] = f2bf(f2(v0, v1));
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) w[e] = f2bf(f2(sv[2 * e], sv[2 * e + 1]));
                 }
               }
+              // P columns 16J + 4cc .. +3 lie over S columns this thread has already read
+              tmem_st4(tS + 16 * J + 4 * cc, w);
             }
-            // P columns 16J .. 16J+15 lie over S columns this thread has already read
-            tmem_st16(tS + 16 * J, w);
           }
           const float scl = sm->scl[s3][i], gam = sm->gam[s3][i];
           const float dg = Dh + (scl > 0.f ? gam * sii * rcp_approx(scl) : 0.f);
