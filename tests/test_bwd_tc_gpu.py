@@ -204,7 +204,8 @@ def test_forward_saved_states_equal_the_recompute_sweep():
         chunk=128, policy_name="bf16")
     out.y.backward(dy)
     for leaf, ref in zip(leaves, (g2.dq, g2.dk, g2.dv)):
-        assert torch.allclose(leaf.grad.float(), ref.to(torch.bfloat16).float(), rtol=2e-2, atol=1e-3)
+        a, b = leaf.grad.double(), ref.double()
+        assert float((a - b).norm() / b.norm()) < 1e-2
 
 
 @pytest.mark.parametrize("kernel", ["tensorcore", "generic"])
