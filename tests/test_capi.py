@@ -130,3 +130,23 @@ def test_sample_validation():
     assert C.lib().m3_sample_tokens(a, None) == C.M3_ERR_ARG  # history without a counter
     a.history, a.batch = None, 0
     assert C.lib().m3_sample_tokens(a, None) == C.M3_OK  # nothing to do
+
+
+def test_jax_ffi_shim_binds_only_exported_entry_points():
+    """The jax.ffi handlers (``jax_ffi/m3_ffi.cc``) cannot be built here (no jaxlib / XLA FFI
+    headers); check that every library call they make is an entry point of the C ABI, and
+    that the Python side refuses to import without JAX instead of failing later."""
+    import importlib
+    import re
+
+    src = open(os.path.join(ROOT, "mamba3-siso-tpu_b200", "jax_ffi", "m3_ffi.cc")).read()
+    header = open(os.path.join(ROOT, "include", "m3_siso.h")).read()
+    calls = set(re.findall(r"\b(m3_[a-z0-9_]+)\(", src))
+    assert calls >= {"m3_siso_fwd", "m3_siso_bwd_noalloc", "m3_siso_decode", "m3_last_error"}
+    for c in calls:
+        assert re.search(rf"\b{c}\s*\(", header), c
+    try:
+        import jax  # noqa: F401
+    except ImportError:
+        with pytest.raises(ImportError):
+            importlib.import_module("jax_ffi")
