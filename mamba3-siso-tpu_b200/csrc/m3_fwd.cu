@@ -72,7 +72,11 @@ static int run_fwd_tc(const M3FwdArgs& a, cudaStream_t s, const tc::TcStates* st
 }
 
 // The backward's recompute sweep: chunk-start state tiles and angle carries only.
+static bool fwd_ws_eligible(const M3FwdArgs& a, bool states_only);
+static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float* phis, bool states_only);
+
 int launch_fwd_states_tc(const M3FwdArgs& a, uint8_t* tiles, float* phis, cudaStream_t s) {
+  if (fwd_ws_eligible(a, true)) return run_fwd_ws(a, s, tiles, phis, true);
   const tc::TcStates st{tiles, phis};
   return run_fwd_tc(a, s, &st);
 }
@@ -112,9 +116,9 @@ static bool make_map(CUtensorMap* m, const void* ptr, int rank, const uint64_t* 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static bool fwd_ws_eligible(const M3FwdArgs& a) {
+static bool fwd_ws_eligible(const M3FwdArgs& a, bool states_only) {
   if (a.kernel == M3_KERNEL_GENERIC || a.kernel == M3_KERNEL_TENSORCORE_V1) return false;
-  if (!a.raw || !a.y || a.ybar || a.chunk_states) return false;
+  if (!a.raw || (!states_only && !a.y) || a.ybar || a.chunk_states) return false;
   if (!fwd_tc_eligible(a)) return false;
   return al16(a.q_bias) && al16(a.k_bias);
 }
@@ -134,7 +138,7 @@ static int sm_count() {
   return c;
 }
 
-static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float* phis) {
+static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float* phis, bool states_only) {
   const M3Dims& d = a.dims;
   CUtensorMap tq, tk, tv, tz, ty;
   const uint64_t dq[3] = {(uint64_t)d.state_dim, (uint64_t)d.seqlen, (uint64_t)d.batch};
@@ -143,7 +147,7 @@ static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float*
   const int64_t sv[3] = {a.v_st.l, a.v_st.h, a.v_st.b}, sy[3] = {a.y_st.l, a.y_st.h, a.y_st.b};
   const int64_t sz[3] = {a.z_st.l, a.z_st.h, a.z_st.b};
   if (!make_map(&tq, a.q, 3, dq, sq) || !make_map(&tk, a.k, 3, dq, sk) || !make_map(&tv, a.v, 4, dv, sv) ||
-      !make_map(&ty, a.y, 4, dv, sy) || !make_map(&tz, a.z ? a.z : a.v, 4, dv, a.z ? sz : sv))
+      !make_map(&ty, states_only ? a.v : a.y, 4, dv, states_only ? sv : sy) || !make_map(&tz, a.z ? a.z : a.v, 4, dv, a.z ? sz : sv))
     return set_error(M3_ERR_LAUNCH, "m3_siso_fwd: cuTensorMapEncodeTiled failed");
   const bool pre = a.fwd_workspace && a.fwd_workspace_bytes >= fwd_workspace_bytes(d) &&
                    ((uintptr_t)a.fwd_workspace % 256) == 0;
@@ -158,14 +162,17 @@ static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float*
     if (rc != M3_OK) return rc;
     ex.T = T;
   }
-  auto* kern = pre ? ws::fwd_ws_kernel<true> : ws::fwd_ws_kernel<false>;
-  static bool attr_done[2][64] = {};
+  decltype(&ws::fwd_ws_kernel<true, false>) kerns[4] = {ws::fwd_ws_kernel<false, false>, ws::fwd_ws_kernel<true, false>,
+                                                         ws::fwd_ws_kernel<false, true>, ws::fwd_ws_kernel<true, true>};
+  const int mode = (pre ? 1 : 0) + (states_only ? 2 : 0);
+  auto* kern = kerns[mode];
+  static bool attr_done[4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[pre][dev]) {
+  if (dev < 64 && !attr_done[mode][dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmemBytes) != cudaSuccess)
       return check_launch("fwd_ws: cudaFuncSetAttribute");
-    attr_done[pre][dev] = true;
+    attr_done[mode][dev] = true;
   }
   const int grid = std::min(nsm, ex.nunits);
   kern<<<grid, ws::kThreads, ws::kSmemBytes, s>>>(a, tq, tk, tv, tz, ty, ex);
@@ -184,6 +191,7 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
   if (!a.y) {  // final state only: the states-only variant of the tensor-core kernel
     if (!tc_ok || a.kernel == M3_KERNEL_GENERIC)
       return set_error(M3_ERR_UNSUPPORTED, "y == NULL (final state only) needs the tensor-core forward");
+    if (fwd_ws_eligible(a, true)) return run_fwd_ws(a, s, nullptr, nullptr, true);
     const tc::TcStates none{nullptr, nullptr};
     return run_fwd_tc(a, s, &none);
   }
@@ -194,7 +202,7 @@ int launch_fwd(const M3FwdArgs& a, cudaStream_t s) {
       tiles = (uint8_t*)a.bwd_states;
       phis = (float*)(tiles + tc_tiles_bytes(a.dims));
     }
-    if (fwd_ws_eligible(a)) return run_fwd_ws(a, s, tiles, phis);
+    if (fwd_ws_eligible(a, false)) return run_fwd_ws(a, s, tiles, phis, false);
     if (tiles) {
       const tc::TcStates save{tiles, phis};
       return run_fwd_tc(a, s, nullptr, &save);

@@ -283,7 +283,9 @@ __global__ void angle_rate_kernel(const float* __restrict__ angles, M3Strides st
   }
 }
 
-template <bool PRE_T>
+// ST: states only -- no y; the k rotation, the state update and the state pass alone (the
+// backward's chunk-start states, or pass 1 of a split over the sequence length).
+template <bool PRE_T, bool ST>
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_ws_kernel(const __grid_constant__ M3FwdArgs a, const __grid_constant__ CUtensorMap tq,
                   const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
@@ -336,13 +338,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int t0 = c * kC;
           // q / k: free once chunk G-2's S, Yi and state update have read them
           if (G >= 2 && !(ok = wait(sm, &sm->mma1[s], ((G - 2) >> 1) & 1, 21))) break;
-          expect_tx(&sm->full_qk[s], 2 * 32768);
-          tma_load3(st + kOQ, &tq, 0, t0, b, &sm->full_qk[s]);
-          tma_load3(st + kOQ + 16384, &tq, 64, t0, b, &sm->full_qk[s]);
+          expect_tx(&sm->full_qk[s], ST ? 32768 : 2 * 32768);
+          if (!ST) {
+            tma_load3(st + kOQ, &tq, 0, t0, b, &sm->full_qk[s]);
+            tma_load3(st + kOQ + 16384, &tq, 64, t0, b, &sm->full_qk[s]);
+          }
           tma_load3(st + kOK, &tk, 0, t0, b, &sm->full_qk[s]);
           tma_load3(st + kOK + 16384, &tk, 64, t0, b, &sm->full_qk[s]);
           // v: free once chunk G-2's Ya has read it
-          if (G >= 2 && !(ok = wait(sm, &sm->mma2[s], ((G - 2) >> 1) & 1, 22))) break;
+          if (!ST && G >= 2 && !(ok = wait(sm, &sm->mma2[s], ((G - 2) >> 1) & 1, 22))) break;
           expect_tx(&sm->full_v[s], 16384);
           tma_load4(st + kOV, &tv, 0, t0, h, b, &sm->full_v[s]);
         }
@@ -395,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = wait(sm, &sm->rot_done[s], (G >> 1) & 1, 32))) break;
           umma::fence_after_sync();
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
+          for (int ks = 0; ks < (ST ? 0 : 8); ++ks) {
             const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
             umma::mma_bf16(tm + kTS + 128 * s, umma::smem_desc(sQ + kmaj, 16, 1024),
                            umma::smem_desc(sK + kmaj, 16, 1024), id_s, ks > 0);
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = wait(sm, &sm->state_ready, G & 1, 33))) break;
           umma::fence_after_sync();
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
+          for (int ks = 0; ks < (ST ? 0 : 8); ++ks) {
             const uint32_t kmaj = (ks >> 2) * 16384u + (ks & 3) * 32u;
             umma::mma_bf16(tm + kTYi + 64 * s, umma::smem_desc(sQ + kmaj, 16, 1024),
                            umma::smem_desc(sST + ks * 2048u, 16384, 1024), id_yi, ks > 0);
@@ -415,9 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                            id_ds, true);
           }
           umma::commit(&sm->mma1[s]);
-          if (c > 0 && !(ok = issue_ya(G - 1))) break;
+          if (!ST && c > 0 && !(ok = issue_ya(G - 1))) break;
         }
-        if (ok && !(ok = issue_ya(G - 1))) break;
+        if (!ST && ok && !(ok = issue_ya(G - 1))) break;
       }
       // every MMA issued has completed before TMEM is freed
       umma::commit(&sm->drain);
@@ -501,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) arrive(&sm->scal_ready[s3]);
       }
     }
-  } else if (warp == 3) {
+  } else if (warp == 3 && !ST) {
     // ================================ y out, z in ===================================
     if (lane == 0) {
       uint32_t G = 0;
@@ -736,8 +740,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok_lo[e] = f2bf(mul2(klo, sc2));
             ok_hi[e] = f2bf(mul2(khi, sc2));
           }
-          *reinterpret_cast<uint4*>(sQ + soff) = make_uint4(oq_lo[0], oq_lo[1], oq_lo[2], oq_lo[3]);
-          *reinterpret_cast<uint4*>(sQ + 16384 + soff) = make_uint4(oq_hi[0], oq_hi[1], oq_hi[2], oq_hi[3]);
+          if (!ST) {
+            *reinterpret_cast<uint4*>(sQ + soff) = make_uint4(oq_lo[0], oq_lo[1], oq_lo[2], oq_lo[3]);
+            *reinterpret_cast<uint4*>(sQ + 16384 + soff) = make_uint4(oq_hi[0], oq_hi[1], oq_hi[2], oq_hi[3]);
+          }
           *reinterpret_cast<uint4*>(sK + soff) = make_uint4(ok_lo[0], ok_lo[1], ok_lo[2], ok_lo[3]);
           *reinterpret_cast<uint4*>(sK + 16384 + soff) = make_uint4(ok_hi[0], ok_hi[1], ok_hi[2], ok_hi[3]);
 #pragma unroll
@@ -750,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         WS_MARK(86);
         // ---- vd = v exp2(A_last - A) for this warp's 16 rows --------------------------
-        if (G >= 2) yok = yok && wait_warp(sm, &sm->yfree[s], ((G - 2) >> 1) & 1, 63);
+        if (!ST && G >= 2) yok = yok && wait_warp(sm, &sm->yfree[s], ((G - 2) >> 1) & 1, 63);
         yok = yok && wait_warp(sm, &sm->full_v[s], (G >> 1) & 1, 64);
         WS_MARK(87);
         {
@@ -926,6 +932,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         WS_MARK(92);
+        if constexpr (ST) {  // no output: the state pass is all; release this chunk's scalars
+          __syncwarp();
+          if (lane == 0) arrive(&sm->scal_free[G % 3]);
+          if (last && a.final_v && i < kP) {
+            const __nv_bfloat16* vr = (const __nv_bfloat16*)a.v + (size_t)b * a.v_st.b + (size_t)h * a.v_st.h +
+                                      (size_t)(L - 1) * a.v_st.l;
+            a.final_v[bh * kP + i] = __bfloat162float(vr[i]);
+          }
+          continue;
+        }
         // ---- output of the previous chunk ------------------------------------------------
         if (c > 0 && !(ok = epilogue(G - 1, c - 1))) break;
         WS_MARK(93);
@@ -1006,7 +1022,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         WS_MARK(94);
       }
       if (!ok) break;
-      if (!(ok = epilogue(G - 1, nchunk - 1))) break;
+      if (!ST && !(ok = epilogue(G - 1, nchunk - 1))) break;
     }
   }
   }

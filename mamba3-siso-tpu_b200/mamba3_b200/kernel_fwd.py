@@ -175,10 +175,10 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
         a.y, a.y_st = T.ptr(y), T.st_bhlp(y)
     a.final_ssm, a.final_k, a.final_v, a.final_phi = T.ptr(fs), T.ptr(fk), T.ptr(fv), T.ptr(fphi)
     a.kernel = _kernel_code(kernel)
-    if y is not None:  # head-shared rotary rates, computed once per (b, t, angle)
-        wsz = C.lib().m3_siso_fwd_workspace_size(ctypes.byref(a.dims))
-        fws = torch.empty(wsz, dtype=torch.uint8, device=dev)
-        a.fwd_workspace, a.fwd_workspace_bytes = T.ptr(fws), wsz
+    # head-shared rotary rates, computed once per (b, t, angle) by the tensor-core forward
+    wsz = C.lib().m3_siso_fwd_workspace_size(ctypes.byref(a.dims))
+    fws = torch.empty(wsz, dtype=torch.uint8, device=dev)
+    a.fwd_workspace, a.fwd_workspace_bytes = T.ptr(fws), wsz
     saved = False
     if bwd_states is not None and C.lib().m3_siso_fwd_saves_states(a):
         a.bwd_states, a.bwd_states_bytes = T.ptr(bwd_states), bwd_states.numel() * bwd_states.element_size()
