@@ -201,6 +201,44 @@ int m3_siso_bwd_noalloc(const M3BwdArgs *args, void *stream);
 size_t m3_siso_bwd_noalloc_scratch_bytes(void);
 
 /* ---------------------------------------------------------------------------------
+ * The forward split over the sequence length (kernel_fwd._forward_raw_split): when a batch
+ * has too few (b, h) sequences to fill the GPU, each is cut into `segments` pieces scanned
+ * side by side.  No counterpart kernel in the reference; the result is its segment chaining
+ * (mamba3_pallas/siso.py:154-216) applied piece after piece.
+ *   prep:  per (b, segment, 64-token tile): partial (B, G, S, H, Nr + 1), S = seqlen /
+ *          (64 G), = the tile's sums of tanh(angles) dt per angle, then of adt; coef (B, G, H)
+ *          = dt (1 - lam) of each segment's first token.  seqlen % (64 G) == 0.
+ *   carry: per (b, h).  With s_loc == NULL (before the states-only pass): partial reduced
+ *          into a_seg (B, G, H) = sum adt per segment and the entering angles phi_in
+ *          (B*G, H, Nr).  With s_loc, from a states-only pass of every segment from a zero
+ *          state at its true angle (s_loc (B*G, H, P, N), k_last (B*G, H, N), v_last
+ *          (B*G, H, P)): the entering c_ssm, c_k, c_v of every segment for the full pass.
+ * ------------------------------------------------------------------------------- */
+#define M3_SPLIT_TILE 64
+
+typedef struct M3SplitPrepArgs {
+  int32_t batch, seqlen, nheads, n_angles, segments;
+  float a_floor;
+  const float *dt_raw, *a_raw, *trap_raw; M3Strides raw_st;   /* (B, L, H), strides as M3FwdArgs */
+  const float *angles;                    M3Strides ang_st;   /* (B, L, Nr) */
+  const float *dt_bias;
+  float *partial, *coef;
+} M3SplitPrepArgs;
+
+typedef struct M3SplitCarryArgs {
+  int32_t batch, nheads, segments, tiles, state_dim, headdim, n_angles;
+  const float *partial;
+  float *a_seg;                                               /* written by the angles-only launch */
+  const float *coef;
+  const float *s_loc, *k_last, *v_last;
+  const float *seed_ssm, *seed_k, *seed_v, *seed_phi;         /* (B, H, ...), each may be NULL */
+  float *phi_in, *c_ssm, *c_k, *c_v;
+} M3SplitCarryArgs;
+
+int m3_siso_split_prep(const M3SplitPrepArgs *args, void *stream);
+int m3_siso_split_carry(const M3SplitCarryArgs *args, void *stream);
+
+/* ---------------------------------------------------------------------------------
  * Single-token decode step.  Replaces kernel_decode.decode_step / siso_decode /
  * siso_decode_folded (mamba3_pallas/kernel_decode.py:252-471).  The state buffers are
  * updated IN PLACE (the reference donates them: kernel_decode.py:350-352, 454).

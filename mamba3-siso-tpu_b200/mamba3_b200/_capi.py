@@ -57,6 +57,21 @@ class M3FwdArgs(ctypes.Structure):
     ]
 
 
+class M3SplitPrepArgs(ctypes.Structure):
+    _fields_ = [("batch", _i32), ("seqlen", _i32), ("nheads", _i32), ("n_angles", _i32), ("segments", _i32),
+                ("a_floor", _f32), ("dt_raw", _vp), ("a_raw", _vp), ("trap_raw", _vp), ("raw_st", M3Strides),
+                ("angles", _vp), ("ang_st", M3Strides), ("dt_bias", _vp), ("partial", _vp), ("coef", _vp)]
+
+
+class M3SplitCarryArgs(ctypes.Structure):
+    _fields_ = [("batch", _i32), ("nheads", _i32), ("segments", _i32), ("tiles", _i32), ("state_dim", _i32),
+                ("headdim", _i32), ("n_angles", _i32), ("partial", _vp), ("a_seg", _vp), ("coef", _vp), ("s_loc", _vp),
+                ("k_last", _vp), ("v_last", _vp), ("seed_ssm", _vp), ("seed_k", _vp), ("seed_v", _vp), ("seed_phi", _vp),
+                ("phi_in", _vp), ("c_ssm", _vp), ("c_k", _vp), ("c_v", _vp)]
+
+
+M3_SPLIT_TILE = 64
+
 M3_KERNEL_AUTO = 0
 M3_KERNEL_GENERIC = 1
 M3_KERNEL_TENSORCORE = 2
@@ -122,7 +137,8 @@ class M3GemvArgs(ctypes.Structure):
 EXPORTS = ("m3_siso_fwd", "m3_siso_fwd_workspace_size", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
            "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
-           "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states", "m3_gated_act_bf16")
+           "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states", "m3_gated_act_bf16", "m3_siso_split_prep",
+           "m3_siso_split_carry")
 
 _lib = None
 
@@ -142,6 +158,10 @@ def lib():
         L.m3_siso_fwd_saves_states.restype = ctypes.c_int
         L.m3_siso_bwd.argtypes = [ctypes.POINTER(M3BwdArgs), _vp]
         L.m3_siso_bwd.restype = ctypes.c_int
+        L.m3_siso_split_prep.argtypes = [ctypes.POINTER(M3SplitPrepArgs), _vp]
+        L.m3_siso_split_prep.restype = ctypes.c_int
+        L.m3_siso_split_carry.argtypes = [ctypes.POINTER(M3SplitCarryArgs), _vp]
+        L.m3_siso_split_carry.restype = ctypes.c_int
         L.m3_siso_fwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]
         L.m3_siso_fwd_workspace_size.restype = ctypes.c_size_t
         L.m3_siso_bwd_workspace_size.argtypes = [ctypes.POINTER(M3Dims)]

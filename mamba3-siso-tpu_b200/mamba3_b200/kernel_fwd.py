@@ -121,7 +121,7 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
                      a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
                      y_out: Optional[torch.Tensor] = None, kernel: str = "auto",
                      bwd_states: Optional[torch.Tensor] = None, return_saved: bool = False,
-                     states_only: bool = False):
+                     states_only: bool = False, lsplit: Optional[int] = None):
     """Fused boundary: raw ``(B, L, H)`` dt/A/trap streams and head-shared ``(B, L, Nr)``
     angles (all may be strided views of an in_proj output).  Returns
     ``(y, final_ssm, final_k, final_v, final_phi)``.  ``y_out`` may be a strided
@@ -131,7 +131,17 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     inputs; when this forward runs on tensor cores it stores the chunk-start states there
     and that backward can pass ``states_ready=True``.  ``return_saved`` appends whether it
     did.  ``states_only``: no y (returned as None), only the final state -- the states-only
-    variant of the tensor-core kernel; see `final_state_supported`."""
+    variant of the tensor-core kernel; see `final_state_supported`.
+
+    ``lsplit``: cut every sequence into that many segments scanned side by side (see
+    `_forward_raw_split`); ``None`` picks it from the SM count when the batch has too few
+    (b, h) sequences to fill the GPU, 1 never splits."""
+    if lsplit is None and not states_only and bwd_states is None and not return_saved:
+        lsplit = _auto_split(q, v, angles, chunk, dtype_policy, kernel)
+    if lsplit is not None and lsplit > 1 and not states_only and bwd_states is None and not return_saved:
+        return _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z,
+                                  seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, dtype_policy, y_out, kernel,
+                                  lsplit)
     L.validate_chunk(chunk)
     T.require_cuda(q, k, v)
     _check_shapes(q, k, v, z)
@@ -195,3 +205,117 @@ def final_state_supported(q, v, angles, chunk: int, dtype_policy: str = "bf16") 
     n, p, nr = q.shape[-1], v.shape[-1], angles.shape[-1]
     return (v.dtype == torch.bfloat16 and T.policy_code(dtype_policy) == C.M3_POLICY_BF16 and n == 128
             and p == 64 and chunk % 128 == 0 and nr % 8 == 0 and nr <= 64 and q.shape[1] % 128 == 0)
+
+
+_MIN_SEGMENT_CHUNKS = 8  # a segment shorter than this spends more on the extra pass than it gains
+_MIN_SEGMENTS = 3  # 2 segments cost 2 x 0.5 x (1 + 0.65) of one pass: no gain
+
+
+def _sm_count(device) -> int:
+    return torch.cuda.get_device_properties(device).multi_processor_count
+
+
+def _auto_split(q, v, angles, chunk, dtype_policy, kernel) -> int:
+    """Segments per sequence so that B * H * segments sequences fill the SMs once: the
+    tensor-core forward runs one sequence per SM at a time.  The split runs a states-only
+    pass (~0.65 of a full pass) before the full one, so it pays from 3 segments on."""
+    if kernel not in ("auto", "tensorcore") or not final_state_supported(q, v, angles, chunk, dtype_policy):
+        return 1
+    units = q.shape[0] * v.shape[1]
+    nsm = _sm_count(q.device)
+    nck = q.shape[1] // chunk
+    best = 1
+    for g in range(2, nck // _MIN_SEGMENT_CHUNKS + 1):
+        if nck % g == 0 and units * g <= nsm:
+            best = g
+    return best if best >= _MIN_SEGMENTS else 1
+
+
+def _split_view(t, g):
+    """(B, L, ...) -> (B * g, L / g, ...) without a copy when the batch stride is L times the
+    token stride (dense or a layer's in_proj slice); else a dense copy first."""
+    b, l = t.shape[0], t.shape[1]
+    if t.stride(0) != l * t.stride(1):
+        t = t.contiguous()
+    return t.as_strided((b * g, l // g) + tuple(t.shape[2:]), (t.stride(1) * (l // g),) + tuple(t.stride()[1:]))
+
+
+def _split_view_bhlp(t, g):
+    """(B, H, L, P) -> (B * g, H, L / g, P) (the same rule on the batch and token strides)."""
+    b, h, l, p = t.shape
+    if t.stride(0) != l * t.stride(2):
+        t = t.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+    return t.as_strided((b * g, h, l // g, p), (t.stride(2) * (l // g), t.stride(1), t.stride(2), t.stride(3)))
+
+
+def _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z,
+                       seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, dtype_policy, y_out, kernel, g):
+    """The forward with every sequence cut into ``g`` segments that run side by side, so a
+    batch of few (b, h) sequences still fills the GPU (one sequence per SM at a time).
+
+    Segment j is scanned as if it were chained after segment j-1 (the reference's
+    segmentation rule, ``siso.py:154-216``: the carried state plus the trapezoid seed term
+    ``dt_0 (1 - lam_0) v_prev k_prev^T``), which equals one scan of the whole sequence.  Its
+    entering carry is rebuilt instead of waited for:
+
+    1. the entering angle of every segment: the carry's phi plus the earlier segments' sums
+       of tanh(angle) pi dt (tile sums by ``m3_siso_split_prep``, reduced by the angles-only
+       ``m3_siso_split_carry``);
+    2. pass 1, states only, from a zero state at that angle: each segment's own final state
+       S_j, and its true last k and v;
+    3. S_end(j) = e^{A_j} (S_end(j-1) + c_j v_{j-1} k_{j-1}^T) + S_j (A_j the segment's sum of
+       adt, c_j = dt (1 - lam) of its first token), serially over the segments by the full
+       ``m3_siso_split_carry``;
+    4. pass 2, the full forward of all segments from their true carries."""
+    b, l, n = q.shape
+    h, p = v.shape[1], v.shape[3]
+    nr = angles.shape[-1]
+    dev, f32 = q.device, torch.float32
+    stream = T.stream_handle(dev)
+    dt_raw, a_raw, trap_raw, angles = (T.f32c(t) for t in (dt_raw, a_raw, trap_raw, angles))
+    if dt_raw.stride() != a_raw.stride() or dt_raw.stride() != trap_raw.stride():
+        dt_raw, a_raw, trap_raw = dt_raw.contiguous(), a_raw.contiguous(), trap_raw.contiguous()
+    dtb = T.f32dense(dt_bias)
+    # 1. per-tile sums of the angle increments and decays, seed coefficients (one kernel)
+    tiles = l // (g * C.M3_SPLIT_TILE)
+    partial = torch.empty(b, g, tiles, h, nr + 1, dtype=f32, device=dev)
+    coef = torch.empty(b, g, h, dtype=f32, device=dev)
+    pa = C.M3SplitPrepArgs(b, l, h, nr, g, a_floor, T.ptr(dt_raw), T.ptr(a_raw), T.ptr(trap_raw), T.st_blh(dt_raw),
+                           T.ptr(angles), T.st_bln(angles), T.ptr(dtb), T.ptr(partial), T.ptr(coef))
+    C.check(C.lib().m3_siso_split_prep(ctypes.byref(pa), stream))
+    # views of every (B, L, ...) input as (B * g, L / g, ...)
+    qs, ks = _split_view(q, g), _split_view(k, g)
+    vs = _split_view_bhlp(v, g)
+    zs = None if z is None else _split_view_bhlp(z, g)
+    raws = [_split_view(t, g) for t in (dt_raw, a_raw, trap_raw, angles)]
+    common = dict(d_skip=d_skip, a_floor=a_floor, chunk=chunk, dtype_policy=dtype_policy, kernel=kernel, lsplit=1)
+    seeds = [None if t is None else T.f32dense(t) for t in (seed_ssm, seed_k, seed_v, seed_phi)]
+    # 2. segment sums and entering angles; pass 1: each segment's own state from zero at its true angle
+    phi_in = torch.empty(b * g, h, nr, dtype=f32, device=dev)
+    a_seg = torch.empty(b, g, h, dtype=f32, device=dev)
+    ca = C.M3SplitCarryArgs(b, h, g, tiles, n, p, nr, T.ptr(partial), T.ptr(a_seg), T.ptr(coef), None, None, None,
+                            *(T.ptr(t) for t in seeds), T.ptr(phi_in), None, None, None)
+    C.check(C.lib().m3_siso_split_carry(ctypes.byref(ca), stream))
+    _, s_loc, k_last, v_last, _ = siso_forward_raw(qs, ks, vs, *raws, dt_bias, q_bias, k_bias, z=zs,
+                                                   seed_phi=phi_in, states_only=True, **common)
+    c_ssm = torch.empty(b * g, h, p, n, dtype=f32, device=dev)
+    c_k = torch.empty(b * g, h, n, dtype=f32, device=dev)
+    c_v = torch.empty(b * g, h, p, dtype=f32, device=dev)
+    ca.c_ssm, ca.c_k, ca.c_v = T.ptr(c_ssm), T.ptr(c_k), T.ptr(c_v)
+    # 3. the entering states, k and v of every segment (one kernel, serial over segments)
+    ca.s_loc, ca.k_last, ca.v_last = T.ptr(s_loc), T.ptr(k_last), T.ptr(v_last)
+    C.check(C.lib().m3_siso_split_carry(ctypes.byref(ca), stream))
+    # 4. pass 2: every segment from its true carry (segment 0 without one if the caller had none)
+    # (a (B, L, H, P) buffer seen as (B, H, L, P) splits without a copy)
+    io = v.dtype if v.dtype in (torch.bfloat16, f32) else f32
+    target = y_out
+    if y_out is None or y_out.stride(0) != l * y_out.stride(2):
+        y_out = torch.empty(b, l, h, p, dtype=io, device=dev).permute(0, 2, 1, 3)
+    ys = _split_view_bhlp(y_out, g)
+    _, fs, fk, fv, fphi = siso_forward_raw(qs, ks, vs, *raws, dt_bias, q_bias, k_bias, z=zs, seed_ssm=c_ssm,
+                                           seed_k=c_k, seed_v=c_v, seed_phi=phi_in, y_out=ys, **common)
+    if target is not None and target.data_ptr() != y_out.data_ptr():
+        target.copy_(y_out)
+        y_out = target
+    last = lambda t: t.unflatten(0, (b, g))[:, g - 1]  # the last segment of every sequence
+    return y_out, last(fs), last(fk), last(fv), last(fphi)
