@@ -247,6 +247,8 @@ def rank_slice(c, world):
 
 
 def bench_fwd(c, steps, warmup, world, rank, peaks):
+    from mamba3_b200 import kernel_fwd as KF
+
     cl = rank_slice(c, world)
     d = make_cfg2_inputs(cl, seed=1000 + rank)
     tokens = c["B"] * c["L"]  # the global batch
@@ -263,7 +265,9 @@ def bench_fwd(c, steps, warmup, world, rank, peaks):
         "bytes": byts,
         "tflops": flops / (per_step / 1e3) / 1e12,
         "gbs": byts / (per_step / 1e3) / 1e9,
-        "launches": 2 * steps,  # the head-shared rotary-rate pass + the forward kernel
+        # the head-shared rotary-rate pass + the forward kernel (+ the length split's kernels
+        # when the per-GPU batch is too small to fill the SMs)
+        "launches": steps * KF.forward_launches(d["q"], d["x"].permute(0, 2, 1, 3), d["angles"], cl["chunk"]),
     }, d
 
 
@@ -318,14 +322,33 @@ def bench_fwd_bwd(c, steps, warmup, world, rank):
                              dtype_policy="bf16", workspace=ws, states_ready=saved)
         return saved
 
+    def step_recompute():  # kernel_bwd.py's scheme: nothing kept from the forward, the sweep recomputes
+        KF.siso_forward_raw(d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                            d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z,
+                            chunk=c["chunk"], dtype_policy="bf16")
+        KB.siso_backward_raw(dy, d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                             d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z, chunk=c["chunk"],
+                             dtype_policy="bf16", workspace=ws, states_ready=False)
+
     saved = step()
     ms = timed(step, steps, warmup, world)
     per = ms / steps
+    step_recompute()
+    per_rc = timed(step_recompute, steps, warmup, world) / steps
     th = c["B"] * c["L"] * c["H"]
     flops = (FWD_FLOP_PER_TOKEN_HEAD + BWD_FLOP_PER_TOKEN_HEAD) * th
+    kept = c["B"] * c["H"] * (c["L"] // c["chunk"] + 1) * (c["N"] * c["P"] * 2 + c["Nr"] * 4)
     return {"tok_s": glob["B"] * glob["L"] / (per / 1e3), "ms_per_step": per,
             "tflops": flops / (per / 1e3) / 1e12,
-            "launches_per_step": 2 if saved else 3}  # fwd (saving the states) + bwd; else + the recompute sweep
+            # fwd (rates + scan, saving the states) + bwd; the recompute path adds the sweep's two
+            "launches_per_step": 3 if saved else 5,
+            "states": "saved by the forward" if saved else "recomputed",
+            "saved_state_bytes": kept if saved else 0,
+            "recompute": {"tok_s": glob["B"] * glob["L"] / (per_rc / 1e3), "ms_per_step": per_rc,
+                          "tflops": flops / (per_rc / 1e3) / 1e12, "launches_per_step": 5,
+                          "saved_state_bytes": 0,
+                          "note": "forward keeps nothing; the backward's states-only sweep recomputes the "
+                                  "chunk-start states (the reference's scheme, kernel_bwd.py:103-355)"}}
 
 
 def bench_layer_cfg0(steps, warmup, world):

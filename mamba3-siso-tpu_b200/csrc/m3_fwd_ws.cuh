@@ -72,6 +72,9 @@ struct Small {
   uint64_t state_ready, drain;
   uint32_t tmem;
   int abort_flag;
+#ifdef M3_WS_TIMING
+  unsigned int tacc[128], tcnt[128];  // per-CTA cycle sums and counts by code
+#endif
 };
 constexpr size_t kSmemBytes = kOSmall + sizeof(Small) + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "more shared memory than a B200 CTA can have");
@@ -138,8 +141,8 @@ __device__ unsigned long long g_ws_wait[2][128];
   do {                                                                        \
     if ((threadIdx.x & 31) == 0) {                                            \
       const long long now_ = clock64();                                       \
-      atomicAdd(&g_ws_wait[0][code], (unsigned long long)(now_ - tmark_));    \
-      atomicAdd(&g_ws_wait[1][code], 1ull);                                   \
+      atomicAdd(&sm->tacc[code], (unsigned int)(now_ - tmark_));              \
+      atomicAdd(&sm->tcnt[code], 1u);                                         \
       tmark_ = now_;                                                          \
     }                                                                         \
   } while (0)
@@ -167,8 +170,8 @@ __device__ __forceinline__ bool wait(Small* sm, uint64_t* mbar, uint32_t parity,
         : "memory");
 #ifdef M3_WS_TIMING
     if (done && (threadIdx.x & 31) == 0) {
-      atomicAdd(&g_ws_wait[0][code], (unsigned long long)(clock64() - t0));
-      atomicAdd(&g_ws_wait[1][code], 1ull);
+      atomicAdd(&sm->tacc[code], (unsigned int)(clock64() - t0));
+      atomicAdd(&sm->tcnt[code], 1u);
     }
 #endif
     if (done) return true;
@@ -319,6 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     sm->abort_flag = 0;
     umma::fence_mbar_init();
   }
+#ifdef M3_WS_TIMING
+  if (threadIdx.x < 128) sm->tacc[threadIdx.x] = sm->tcnt[threadIdx.x] = 0u;
+#endif
   if (warp == 1) umma::tmem_alloc(&sm->tmem, 512);
   umma::fence_before_sync();
   __syncthreads();
@@ -1030,6 +1036,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 1) umma::tmem_dealloc(tm, 512);
+#ifdef M3_WS_TIMING
+  if (threadIdx.x < 128 && sm->tcnt[threadIdx.x]) {
+    atomicAdd(&g_ws_wait[0][threadIdx.x], (unsigned long long)sm->tacc[threadIdx.x]);
+    atomicAdd(&g_ws_wait[1][threadIdx.x], (unsigned long long)sm->tcnt[threadIdx.x]);
+  }
+#endif
 }
 
 }  // namespace ws

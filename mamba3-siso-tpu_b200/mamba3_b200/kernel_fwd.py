@@ -231,6 +231,19 @@ def _auto_split(q, v, angles, chunk, dtype_policy, kernel) -> int:
     return best if best >= _MIN_SEGMENTS else 1
 
 
+def forward_launches(q, v, angles, chunk, dtype_policy="bf16", kernel="auto", lsplit=None) -> int:
+    """Kernel launches of one `siso_forward_raw` call with these shapes (no saved states):
+    2 for the tensor-core forward (head-shared rotary rates + the scan), 7 when it is split
+    over the length (tile sums, entering angles, the states-only and the full pass with
+    their rate passes, the carry rebuild), 1 for the generic kernel."""
+    g = _auto_split(q, v, angles, chunk, dtype_policy, kernel) if lsplit is None else lsplit
+    if g > 1:
+        return 7
+    tc = kernel in ("auto", "tensorcore", "tensorcore_v1") and final_state_supported(q, v, angles, chunk,
+                                                                                       dtype_policy)
+    return 2 if tc else 1
+
+
 def _split_view(t, g):
     """(B, L, ...) -> (B * g, L / g, ...) without a copy when the batch stride is L times the
     token stride (dense or a layer's in_proj slice); else a dense copy first."""
