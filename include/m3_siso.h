@@ -320,6 +320,28 @@ typedef struct M3GemvArgs {
 } M3GemvArgs;
 
 int m3_gemv_bf16(const M3GemvArgs *args, void *stream);
+
+/* ---------------------------------------------------------------------------------
+ * Skinny GEMM for the decode step's projections at batch > 8 (the matmul / addmm calls of
+ * model.lm_decode_step, mamba3_pallas/model.py:244-296): out (m, n) bf16 =
+ * [residual +] a (m, k) bf16 @ w, m <= 256, fp32 accumulation, one bf16 rounding.
+ * w_kmajor == 0: w is (k, n), row stride ldw (>= n); w_kmajor == 1: w is (n, k) with k
+ * contiguous (the tied head, embed^T).  k % 64 == 0, n % 8 == 0; a and w 16-byte aligned
+ * with 16-byte row strides, out / residual 8-byte aligned.  Strides in elements, 0 = dense.
+ * residual may equal out (in-place residual add).  Deterministic: K splits are summed in a
+ * fixed order.
+ * ------------------------------------------------------------------------------- */
+typedef struct M3GemmArgs {
+  int32_t m, n, k, w_kmajor;
+  int32_t ksplit;       /* CTAs sharing K in a cluster: 0 = chosen here, else 1, 2 or 4 */
+  int32_t reserved;
+  const void *a;        int64_t lda;
+  const void *w;        int64_t ldw;
+  const void *residual; int64_t ldr;   /* NULL = none */
+  void *out;            int64_t ldo;
+} M3GemmArgs;
+
+int m3_gemm_bf16(const M3GemmArgs *args, void *stream);
 size_t m3_gemv_scratch_floats(int32_t m, int32_t k, int32_t n);
 
 /* ---------------------------------------------------------------------------------

@@ -181,8 +181,8 @@ int m3_sample_tokens(const M3SampleArgs* args, void* stream) {
 }
 
 int m3_device_error(int reset) {
-  const int f = read_device_error(reset), d = read_decode_error(reset);
-  return f != 0 ? f : d;
+  const int f = read_device_error(reset), d = read_decode_error(reset), g = read_gemm_error(reset);
+  return f != 0 ? f : d != 0 ? d : g;
 }
 
 static void fwd_defaults(M3FwdArgs& a) {

@@ -20,6 +20,7 @@ bool supported_np(int n, int p);
 int launch_fwd(const M3FwdArgs& a, cudaStream_t s);
 int read_device_error(int reset);
 int read_decode_error(int reset);
+int read_gemm_error(int reset);
 int launch_rms_norm(const void* x, int64_t xs, const void* w, void* y, int64_t ys, int64_t rows, int dim, float eps,
                     int x_dtype, int w_dtype, float* rstd, cudaStream_t s);
 int launch_rms_norm_bwd(const void* x, int64_t xs, const void* w, const float* rstd, const void* dy, int64_t dys,

@@ -134,11 +134,19 @@ class M3GemvArgs(ctypes.Structure):
     ]
 
 
+class M3GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", _i32), ("n", _i32), ("k", _i32), ("w_kmajor", _i32), ("ksplit", _i32), ("reserved", _i32),
+        ("a", _vp), ("lda", _i64), ("w", _vp),
+        ("ldw", _i64), ("residual", _vp), ("ldr", _i64), ("out", _vp), ("ldo", _i64),
+    ]
+
+
 EXPORTS = ("m3_siso_fwd", "m3_siso_fwd_workspace_size", "m3_siso_bwd", "m3_siso_bwd_workspace_size", "m3_siso_decode",
            "m3_last_error", "m3_version", "m3_siso_bwd_noalloc", "m3_siso_bwd_noalloc_scratch_bytes",
            "m3_device_error", "m3_copy2d_async", "m3_rms_norm", "m3_rms_norm_bwd", "m3_sample_tokens", "m3_gemv_bf16",
            "m3_gemv_scratch_floats", "m3_siso_fwd_saves_states", "m3_gated_act_bf16", "m3_siso_split_prep",
-           "m3_siso_split_carry")
+           "m3_siso_split_carry", "m3_gemm_bf16")
 
 _lib = None
 
@@ -180,6 +188,8 @@ def lib():
         L.m3_gated_act_bf16.restype = ctypes.c_int
         L.m3_gemv_bf16.argtypes = [ctypes.POINTER(M3GemvArgs), _vp]
         L.m3_gemv_bf16.restype = ctypes.c_int
+        L.m3_gemm_bf16.argtypes = [ctypes.POINTER(M3GemmArgs), _vp]
+        L.m3_gemm_bf16.restype = ctypes.c_int
         L.m3_gemv_scratch_floats.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
         L.m3_gemv_scratch_floats.restype = ctypes.c_size_t
         L.m3_copy2d_async.argtypes = [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, _vp]

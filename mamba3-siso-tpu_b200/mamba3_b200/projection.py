@@ -1,4 +1,4 @@
-"""Small-batch projections of the decode step through ``m3_gemv_bf16``.
+"""Projections of the decode step: ``m3_gemv_bf16`` at batch 1, ``m3_gemm_bf16`` up to 256 rows.
 
 At batch 1 (`train.generate`) each projection of `model.lm_decode_step` (``model.py:244-296``)
 is a stream of its bf16 weight; `small_proj` reads it near HBM speed and folds in the
@@ -78,3 +78,45 @@ def gated_act(h: torch.Tensor) -> torch.Tensor:
         return out
     value, gate = h.chunk(2, dim=-1)
     return value * torch.nn.functional.silu(gate)
+
+
+GEMM_MAX_ROWS = 256
+
+
+def gemm_eligible(x: torch.Tensor, w: torch.Tensor, w_kmajor: bool = False) -> bool:
+    """Whether `gemm` takes ``x (m, k) @ w`` (bf16, m <= 256, k % 64 == 0, n % 8 == 0,
+    16-byte rows).  ``w`` is ``(k, n)`` with n contiguous, or with ``w_kmajor`` a ``(k, n)``
+    view of an ``(n, k)`` tensor with k contiguous (``embed.t()``)."""
+    if not (x.is_cuda and x.dim() == 2 and w.dim() == 2 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16):
+        return False
+    m, k = x.shape
+    n = w.shape[1]
+    if not (0 < m <= GEMM_MAX_ROWS and w.shape[0] == k and k % 64 == 0 and n % 8 == 0 and x.stride(1) == 1):
+        return False
+    ldw = w.stride(1) if w_kmajor else w.stride(0)
+    inner = w.stride(0) if w_kmajor else w.stride(1)
+    return (inner == 1 and ldw % 8 == 0 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0
+            and w.data_ptr() % 16 == 0)
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, *, residual: Optional[torch.Tensor] = None, w_kmajor: bool = False,
+         out: Optional[torch.Tensor] = None, ksplit: int = 0) -> torch.Tensor:
+    """``[residual +] x @ w`` for bf16 ``x (m, k)``, ``m <= 256`` (`gemm_eligible`), through the
+    skinny tcgen05 GEMM (``m3_gemm_bf16``): fp32 accumulation, one bf16 rounding, the same
+    result every call.  ``w_kmajor``: ``w`` is ``embed.t()``-like (k contiguous)."""
+    m, k = x.shape
+    n = w.shape[1]
+    if residual is not None and (residual.dtype != torch.bfloat16 or residual.stride(1) != 1
+                                 or residual.stride(0) % 4 or residual.data_ptr() % 8):
+        residual = residual.to(torch.bfloat16).contiguous()
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    a = C.M3GemmArgs()
+    a.m, a.n, a.k, a.w_kmajor, a.ksplit = m, n, k, int(w_kmajor), ksplit
+    a.a, a.lda = T.ptr(x), x.stride(0)
+    a.w, a.ldw = T.ptr(w), (w.stride(1) if w_kmajor else w.stride(0))
+    if residual is not None:
+        a.residual, a.ldr = T.ptr(residual), residual.stride(0)
+    a.out, a.ldo = T.ptr(out), out.stride(0)
+    C.check(C.lib().m3_gemm_bf16(a, T.stream_handle(x.device)))
+    return out

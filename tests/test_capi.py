@@ -42,6 +42,10 @@ int main(void) {
          offsetof(M3DecodeArgs, y));
   printf("%zu %zu %zu %zu\n", sizeof(M3SampleArgs), offsetof(M3SampleArgs, seed), offsetof(M3SampleArgs, stop_ids),
          offsetof(M3SampleArgs, probs_ld));
+  printf("%zu %zu %zu %zu\n", sizeof(M3SplitPrepArgs), offsetof(M3SplitPrepArgs, coef), sizeof(M3SplitCarryArgs),
+         offsetof(M3SplitCarryArgs, c_v));
+  printf("%zu %zu %zu %zu\n", sizeof(M3GemvArgs), offsetof(M3GemvArgs, tickets), sizeof(M3GemmArgs),
+         offsetof(M3GemmArgs, ldo));
   return 0;
 }
 '''
@@ -56,7 +60,11 @@ int main(void) {
             ctypes.sizeof(C.M3BwdArgs), ctypes.sizeof(C.M3DecodeArgs),
             C.M3FwdArgs.chunk_states_dtype.offset, C.M3BwdArgs.workspace_bytes.offset, C.M3DecodeArgs.y.offset,
             ctypes.sizeof(C.M3SampleArgs), C.M3SampleArgs.seed.offset, C.M3SampleArgs.stop_ids.offset,
-            C.M3SampleArgs.probs_ld.offset]
+            C.M3SampleArgs.probs_ld.offset,
+            ctypes.sizeof(C.M3SplitPrepArgs), C.M3SplitPrepArgs.coef.offset, ctypes.sizeof(C.M3SplitCarryArgs),
+            C.M3SplitCarryArgs.c_v.offset,
+            ctypes.sizeof(C.M3GemvArgs), C.M3GemvArgs.tickets.offset, ctypes.sizeof(C.M3GemmArgs),
+            C.M3GemmArgs.ldo.offset]
     assert got == want
 
 
