@@ -77,17 +77,41 @@ __global__ void __launch_bounds__(kPrepThreads) split_prep_kernel(M3SplitPrepArg
   }
   __syncthreads();
   float* out = a.partial + (((size_t)b * G + g) * S + s) * H * (Nr + 1);
-  for (int o = threadIdx.x; o < H * (Nr + 1); o += blockDim.x) {
-    const int h = o / (Nr + 1), r = o % (Nr + 1);
-    float acc = 0.f;
-    if (r < Nr) {
+  if (Nr % 4 == 0) {
+    // thread = (head, 4 consecutive angles): one 128-bit read of tanh per 4 FMAs
+    const int nq = Nr / 4;
+    for (int o = threadIdx.x; o < H * nq; o += blockDim.x) {
+      const int h = o / nq, r4 = 4 * (o % nq);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int t = 0; t < kSplitTile; ++t) {
+        const float4 x = *reinterpret_cast<const float4*>(th + t * Nr + r4);
+        const float d = dt[t * H + h];
+        acc.x = fmaf(x.x, d, acc.x);
+        acc.y = fmaf(x.y, d, acc.y);
+        acc.z = fmaf(x.z, d, acc.z);
+        acc.w = fmaf(x.w, d, acc.w);
+      }
+      float* dst = out + h * (Nr + 1) + r4;
+      dst[0] = acc.x;
+      dst[1] = acc.y;
+      dst[2] = acc.z;
+      dst[3] = acc.w;
+    }
+  } else {
+    for (int o = threadIdx.x; o < H * Nr; o += blockDim.x) {
+      const int h = o / Nr, r = o % Nr;
+      float acc = 0.f;
 #pragma unroll 8
       for (int t = 0; t < kSplitTile; ++t) acc = fmaf(th[t * Nr + r], dt[t * H + h], acc);
-    } else {
-#pragma unroll 8
-      for (int t = 0; t < kSplitTile; ++t) acc += adt[t * H + h];
+      out[h * (Nr + 1) + r] = acc;
     }
-    out[o] = acc;
+  }
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int t = 0; t < kSplitTile; ++t) acc += adt[t * H + h];
+    out[h * (Nr + 1) + Nr] = acc;
   }
 }
 
