@@ -728,6 +728,13 @@ def run_profile_case(which):
                                d_skip=r(H), z=r(B, H, P, dt=torch.bfloat16), dtype_policy="bf16")
         torch.cuda.synchronize()
         return 0
+    if which == "fwdsplit":  # one rank's share at --gpus 8: B = 1, full L, the length split
+        c = dict(CFG2, B=1)
+        d = make_cfg2_inputs(c, 0)
+        for _ in range(3):
+            fwd_call(d, c)
+        torch.cuda.synchronize()
+        return 0
     c = dict(CFG2, L=2048)
     d = make_cfg2_inputs(c, 0)
     if which == "fwd":
@@ -755,7 +762,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all",
                     help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu,seqpar (N > 1) or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdbwd", "decode", "decodestep", "trainstep", "generate"],
+    ap.add_argument("--profile", choices=["fwd", "fwdsplit", "fwdbwd", "decode", "decodestep", "trainstep",
+                                          "generate"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()
