@@ -901,12 +901,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             float stv[32];
             tmem_ld32(tm + lrow + kTSt + 32 * hh, stv);
             umma::tmem_wait_ld();
-            if (!last || saving) {
+            // the bf16 tile is the B operand of the next chunk's Yi (none in states-only mode)
+            // and what the backward reads when the states are saved
+            if ((!ST && !last) || saving) {
               uint4 rowv[4];
 #pragma unroll
               for (int cc = 0; cc < 4; ++cc) {
                 rowv[cc] = tc_pack8(stv + 8 * cc);
-                if (!last) *reinterpret_cast<uint4*>(sST + umma::sw128_off(i, 4 * hh + cc)) = rowv[cc];
+                if (!ST && !last) *reinterpret_cast<uint4*>(sST + umma::sw128_off(i, 4 * hh + cc)) = rowv[cc];
               }
               if (saving) {
                 uint8_t* dst = ex.tiles + (bh * (nchunk + 1) + c + 1) * 16384u;
