@@ -209,6 +209,7 @@ def final_state_supported(q, v, angles, chunk: int, dtype_policy: str = "bf16") 
 
 _MIN_SEGMENT_CHUNKS = 8  # a segment shorter than this spends more on the extra pass than it gains
 _MIN_SEGMENTS = 3  # 2 segments cost 2 x 0.5 x (1 + 0.65) of one pass: no gain
+_MAX_SEGMENTS = 64  # m3_siso_split_carry's limit
 
 
 def _sm_count(device) -> int:
@@ -225,7 +226,7 @@ def _auto_split(q, v, angles, chunk, dtype_policy, kernel) -> int:
     nsm = _sm_count(q.device)
     nck = q.shape[1] // chunk
     best = 1
-    for g in range(2, nck // _MIN_SEGMENT_CHUNKS + 1):
+    for g in range(2, min(nck // _MIN_SEGMENT_CHUNKS, _MAX_SEGMENTS) + 1):
         if nck % g == 0 and units * g <= nsm:
             best = g
     return best if best >= _MIN_SEGMENTS else 1
@@ -283,6 +284,11 @@ def _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias
     b, l, n = q.shape
     h, p = v.shape[1], v.shape[3]
     nr = angles.shape[-1]
+    if not final_state_supported(q, v, angles, chunk, dtype_policy):
+        raise ValueError("lsplit > 1 needs the tensor-core forward (bf16, N = 128, P = 64, chunk % 128 == 0)")
+    if g > _MAX_SEGMENTS or l % (chunk * g):
+        raise ValueError(f"lsplit = {g}: the chunk count {l // chunk} must split into at most "
+                         f"{_MAX_SEGMENTS} equal segments")
     dev, f32 = q.device, torch.float32
     stream = T.stream_handle(dev)
     dt_raw, a_raw, trap_raw, angles = (T.f32c(t) for t in (dt_raw, a_raw, trap_raw, angles))
