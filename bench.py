@@ -728,6 +728,42 @@ def run_profile_case(which):
                                d_skip=r(H), z=r(B, H, P, dt=torch.bfloat16), dtype_policy="bf16")
         torch.cuda.synchronize()
         return 0
+    if which == "bwdphases":  # needs a library built with -DM3_TC_TIMING (diagnostic)
+        import ctypes
+        from mamba3_b200 import _capi as C
+        from mamba3_b200 import kernel_bwd as KB
+        from mamba3_b200 import kernel_fwd as KF
+        lib = C.lib()
+        if not hasattr(lib, "m3_debug_tc_timing"):
+            raise SystemExit("bwdphases: rebuild with build.build(force=True, extra=['-DM3_TC_TIMING'])")
+        lib.m3_debug_tc_timing.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), ctypes.c_int]
+        c = dict(CFG2)
+        d = make_cfg2_inputs(c, 0)
+        ws = torch.empty(KB.workspace_bytes(c["B"], c["L"], c["H"], c["N"], c["P"], c["Nr"], c["chunk"]),
+                         dtype=torch.uint8, device="cuda")
+        v, z, dy = (d[n].permute(0, 2, 1, 3) for n in ("x", "z", "dy"))
+
+        def step():
+            _, saved = KF.siso_forward_raw(d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                                           d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z,
+                                           chunk=c["chunk"], dtype_policy="bf16", bwd_states=ws, return_saved=True)
+            KB.siso_backward_raw(dy, d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                                 d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z, chunk=c["chunk"],
+                                 dtype_policy="bf16", workspace=ws, states_ready=saved)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        buf = (ctypes.c_ulonglong * 24)()
+        lib.m3_debug_tc_timing(buf, 1)
+        step()
+        torch.cuda.synchronize()
+        lib.m3_debug_tc_timing(buf, 1)
+        marks = c["B"] * c["H"] * (c["L"] // c["chunk"])  # thread 0 of each CTA, once per chunk
+        for i in range(24):
+            if buf[i]:
+                print(f"phase {i:2d}: {buf[i] / marks:9.0f} cycles per chunk")
+        return 0
     if which == "fwdsplit":  # one rank's share at --gpus 8: B = 1, full L, the length split
         c = dict(CFG2, B=1)
         d = make_cfg2_inputs(c, 0)
@@ -762,8 +798,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all",
                     help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu,seqpar (N > 1) or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdsplit", "fwdbwd", "decode", "decodestep", "trainstep",
-                                          "generate"],
+    ap.add_argument("--profile", choices=["fwd", "fwdsplit", "fwdbwd", "bwdphases", "decode", "decodestep",
+                                          "trainstep", "generate"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()
