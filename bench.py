@@ -728,6 +728,27 @@ def run_profile_case(which):
                                d_skip=r(H), z=r(B, H, P, dt=torch.bfloat16), dtype_policy="bf16")
         torch.cuda.synchronize()
         return 0
+    if which == "fwdphases":  # needs a library built with -DM3_WS_TIMING (diagnostic)
+        import ctypes
+        from mamba3_b200 import _capi as C
+        lib = C.lib()
+        if not hasattr(lib, "m3_debug_ws_timing"):
+            raise SystemExit("fwdphases: rebuild with build.build(force=True, extra=['-DM3_WS_TIMING'])")
+        lib.m3_debug_ws_timing.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), ctypes.c_int]
+        c = dict(CFG2)
+        d = make_cfg2_inputs(c, 0)
+        for _ in range(3):
+            fwd_call(d, c)
+        torch.cuda.synchronize()
+        buf = (ctypes.c_ulonglong * 256)()
+        lib.m3_debug_ws_timing(buf, 1)
+        fwd_call(d, c)
+        torch.cuda.synchronize()
+        lib.m3_debug_ws_timing(buf, 1)
+        for code in range(128):  # per code: cycles per call (a wait site or a phase of one role)
+            if buf[128 + code]:
+                print(f"code {code:3d}: {buf[code] / buf[128 + code]:9.1f} cycles over {buf[128 + code]} calls")
+        return 0
     if which == "bwdphases":  # needs a library built with -DM3_TC_TIMING (diagnostic)
         import ctypes
         from mamba3_b200 import _capi as C
@@ -798,8 +819,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--what", default="all",
                     help="comma list of fwd,e2e,fwdbwd,decode,train,layer,cpu,seqpar (N > 1) or all")
-    ap.add_argument("--profile", choices=["fwd", "fwdsplit", "fwdbwd", "bwdphases", "decode", "decodestep",
-                                          "trainstep", "generate"],
+    ap.add_argument("--profile", choices=["fwd", "fwdsplit", "fwdphases", "fwdbwd", "bwdphases", "decode",
+                                          "decodestep", "trainstep", "generate"],
                     help="run the small profiling case (configs[1] shapes at L=2048, or one decode layer "
                          "at configs[3]) three times and exit; for ncu captures, prints no bench line")
     args = ap.parse_args()
