@@ -840,6 +840,9 @@ def main():
     c = dict(CFG2)
     torch.backends.cuda.matmul.allow_tf32 = False
     out = {}
+    # the CPU baseline first, on an idle host and before any GPU work, the way the reference
+    # arm (a fresh process) takes it
+    cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
     with ClockSampler(torch.cuda.current_device()) as clk:
         fwd, _ = bench_fwd(c, args.steps, args.warmup, world, rank, peaks)
         if "e2e" in what:
@@ -855,7 +858,6 @@ def main():
         if "seqpar" in what and world > 1:
             out["seqpar"] = bench_seqpar(c, max(2, args.steps // 2), args.warmup, world, rank)
     clocks = clk.summary()
-    cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
 
     if rank != 0:
         return 0
