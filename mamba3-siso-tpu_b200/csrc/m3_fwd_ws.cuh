@@ -847,29 +847,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma::fence_after_sync();
         if (a.z && !wait_warp(sm, &sm->zfull[se], (Ge >> 1) & 1, 73)) return false;
 #pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {  // 8 output columns at a time
-          float acc[8];
-          tmem_ld8(tm + lrow + kTAcc + 8 * cc, acc);
-          const uint32_t off = umma::sw128_off(i, cc);
-          uint32_t zw[4] = {0u, 0u, 0u, 0u};
+        for (int c2 = 0; c2 < 4; ++c2) {  // 16 output columns at a time: two TMEM loads per wait
+          float acc[2][8];
+          tmem_ld8(tm + lrow + kTAcc + 16 * c2, acc[0]);
+          tmem_ld8(tm + lrow + kTAcc + 16 * c2 + 8, acc[1]);
+          uint32_t zw[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
           if (a.z) {
-            const uint4 zz = *reinterpret_cast<const uint4*>(vd + off);
-            zw[0] = zz.x; zw[1] = zz.y; zw[2] = zz.z; zw[3] = zz.w;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint4 zz = *reinterpret_cast<const uint4*>(vd + umma::sw128_off(i, 2 * c2 + hh));
+              zw[hh][0] = zz.x; zw[hh][1] = zz.y; zw[hh][2] = zz.z; zw[hh][3] = zz.w;
+            }
           }
           umma::tmem_wait_ld();
-          uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 o = f2(acc[2 * e], acc[2 * e + 1]);
-            if (a.z) {
-              const float2 zf = bf2f(zw[e]);
-              // silu(z) = z sigmoid(z) = z (0.5 + 0.5 tanh(z / 2))
-              const float2 th = f2(tanh_approx(0.5f * zf.x), tanh_approx(0.5f * zf.y));
-              o = mul2(o, mul2(zf, fma2(th, f2s(0.5f), f2s(0.5f))));
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 o = f2(acc[hh][2 * e], acc[hh][2 * e + 1]);
+              if (a.z) {
+                const float2 zf = bf2f(zw[hh][e]);
+                // silu(z) = z sigmoid(z) = z (0.5 + 0.5 tanh(z / 2))
+                const float2 th = f2(tanh_approx(0.5f * zf.x), tanh_approx(0.5f * zf.y));
+                o = mul2(o, mul2(zf, fma2(th, f2s(0.5f), f2s(0.5f))));
+              }
+              w[e] = f2bf(o);
             }
-            w[e] = f2bf(o);
+            *reinterpret_cast<uint4*>(vd + umma::sw128_off(i, 2 * c2 + hh)) = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          *reinterpret_cast<uint4*>(vd + off) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         umma::fence_async_smem();
         umma::fence_before_sync();
