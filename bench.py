@@ -142,6 +142,34 @@ class ClockSampler:
 # ----------------------------------------------------------------------------------------
 
 
+def bind_to_gpu_cpus(dev_index: int) -> None:
+    """Run this process on the host CPUs local to its GPU (NVML's CPU affinity), so the pinned
+    host buffers of the end-to-end section are allocated on the GPU's NUMA node (first
+    touch) and each rank's copies take its own socket's path.  Best effort: unchanged when
+    NVML or the affinity call is unavailable."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(dev_index)
+            if hasattr(pr, "pci_bus_id"):  # CUDA and NVML may number the GPUs differently
+                bus = "{:08x}:{:02x}:{:02x}.0".format(pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            else:
+                h = pynvml.nvmlDeviceGetHandleByIndex(dev_index)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+            cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (w >> b) & 1}
+            cpus &= set(range(os.cpu_count()))
+            if cpus:
+                os.sched_setaffinity(0, cpus)
+                print(f"bench: GPU {dev_index} -> {len(cpus)} local CPUs", file=sys.stderr)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:
+        pass
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -843,6 +871,9 @@ def main():
     # the CPU baseline first, on an idle host and before any GPU work, the way the reference
     # arm (a fresh process) takes it
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
+    # then the host side of every section on the CPUs local to this rank's GPU
+    bind_to_gpu_cpus(torch.cuda.current_device())
+    torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
     with ClockSampler(torch.cuda.current_device()) as clk:
         fwd, _ = bench_fwd(c, args.steps, args.warmup, world, rank, peaks)
         if "e2e" in what:
