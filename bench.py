@@ -29,6 +29,7 @@ the reference's own Pallas-interpret / reference.py path cannot run) on rank 0.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -66,18 +67,38 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
+TRAFFIC_SOURCES = ("m3_fwd_ws.cuh", "m3_chunk_common.cuh", "m3_umma.cuh", "m3_fwd.cu", "m3_common.cuh")
+
+
+def kernel_source_hash(files=TRAFFIC_SOURCES):
+    """Short sha256 over the forward kernel's source files (what a traffic capture is tied to)."""
+    h = hashlib.sha256()
+    for f in files:
+        h.update(open(os.path.join(ROOT, "mamba3-siso-tpu_b200", "csrc", f), "rb").read())
+    return h.hexdigest()[:16]
+
+
 def load_traffic():
-    """Per-launch DRAM bytes of the profiled kernels (from ncu), if a summary exists."""
+    """Per-launch DRAM bytes of the profiled kernels (from one ncu capture), keyed by kernel.
+
+    A line reads `<kernel> <bytes> src=<hash>`: the hash of the kernel sources the capture was
+    taken with.  A figure whose hash differs from the sources being benched is stale and is
+    returned as None, so the bench line never carries traffic of another build."""
     p = os.path.join(ROOT, "profiles", "traffic.txt")
     out = {}
-    if os.path.exists(p):
-        for line in open(p):
-            parts = line.split()
-            if len(parts) >= 2 and not line.startswith("#"):
-                try:
-                    out[parts[0]] = float(parts[1])
-                except ValueError:
-                    pass
+    if not os.path.exists(p):
+        return out
+    cur = kernel_source_hash()
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 2 and not line.startswith("#"):
+            try:
+                val = float(parts[1])
+            except ValueError:
+                continue
+            src = next((x[4:] for x in parts[2:] if x.startswith("src=")), None)
+            out[parts[0]] = {"bytes": val if src == cur else None, "src": src,
+                             "status": "current" if src == cur else "stale (kernel sources changed since the capture)"}
     return out
 
 
@@ -918,7 +939,8 @@ def main():
                           if per_rank_stream_bytes(dict(c, B=c["B"] // world)) >= 2 * L2_BYTES
                           else "L2 flushed (256 MB write) before every step, outside the timed events")},
         "roofline": {"bound": "hbm", "achieved": fwd["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": hbm_frac, "traffic": traffic.get(kname),
+                     "frac": hbm_frac, "traffic": (traffic.get(kname) or {}).get("bytes"),
+                     "traffic_capture": (traffic.get(kname) or {}).get("status", "no capture"),
                      "peak_src": peaks["src"],
                      "algorithmic_bytes_per_launch": fwd["bytes"],
                      "tensor": {"achieved_tflops": fwd["tflops"], "peak_tflops": peaks["bf16_tflops"],

@@ -124,7 +124,7 @@ def load(path: str, dtype: torch.dtype = None, device="cpu") -> Tuple[M.LMParams
         got: Dict[str, torch.Tensor] = {}
         for (name, ref) in flat_params(template):
             if name not in z.files:
-                raise ValueError(f"{path} is missing array {name!r}")
+                raise ValueError(f"parameter {name!r} not found in {path}")
             a = z[name]
             if tuple(a.shape) != tuple(ref.shape):
                 raise ValueError(f"{name}: checkpoint has shape {a.shape}, config implies {tuple(ref.shape)}")
@@ -137,7 +137,7 @@ def load(path: str, dtype: torch.dtype = None, device="cpu") -> Tuple[M.LMParams
             got[name] = t.to(device=device, dtype=dtype if dtype is not None else t.dtype)
         extra = set(z.files) - {CONFIG_KEY} - set(names)
         if extra:
-            raise ValueError(f"{path} has unexpected arrays: {sorted(extra)}")
+            raise ValueError(f"{path} holds arrays the config does not account for: {sorted(extra)}")
     blocks = []
     for i, b in enumerate(template.blocks):
         siso = LY.SISOParams(*(got[f"blocks.{i}.siso.{f}"] for f in LY.SISOParams._fields))
