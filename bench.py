@@ -15,7 +15,9 @@ in HBM and larger than L2 (nothing is cached between steps).  The same line carr
 * ``decode``    -- the 24-layer LM decode step at B=256: us/token, plus
                    the decode kernel's own HBM roofline;
 * ``cpu_baseline`` -- the CPU oracle restatement of the reference (``oracle/``) timed on
-                   this host's cores on a bounded sample of the forward workload.
+                   this host's cores on a bounded sample of the forward workload;
+* ``torch_ref_baseline`` -- beside it, the reference's own plain-torch recurrent
+                   reference (``torch_ref.mamba3_siso_ref``, from baseline/_ref when installed).
 
 Multi-GPU (torchrun): strong scaling.  configs[1]'s batch of 8 sequences x 32 heads is
 split over the ranks by batch (B / N per rank, all heads), configs[3]'s decode batch of
@@ -23,7 +25,8 @@ split over the ranks by batch (B / N per rank, all heads), configs[3]'s decode b
 are independent, so there is no collective on the scan's data path.  ``value`` is the
 global problem's tokens over the slowest rank's device time.
 ``--impl reference`` times the reference's CPU path (the oracle port; JAX is absent, so
-the reference's own Pallas-interpret / reference.py path cannot run) on rank 0.
+the reference's own Pallas-interpret / reference.py path cannot run) on rank 0, and the
+reference's ``torch_ref.py`` beside it.
 """
 
 from __future__ import annotations
@@ -666,10 +669,64 @@ def cpu_baseline_sample(threads=None, seconds=10.0):
             "sample": f"oracle siso_segment fp32, B=1 H=32 L=1024 N=128 P=64 Nr=64 chunk=128, {n} runs in {el:.1f}s"}
 
 
+REF_TORCH = os.path.join(ROOT, "baseline", "_ref", "mamba3_pallas", "torch_ref.py")
+
+
+def ref_torch_sample(threads=None, seconds=10.0, L=256):
+    """The reference's own CPU code for the path: ``mamba3_siso_ref`` of the installed
+    reference's ``torch_ref.py`` (plain torch; the package's ``__init__`` needs JAX, so the
+    file is loaded on its own), unmodified, on a bounded slice of configs[1]'s forward: all
+    32 heads, N=128 P=64 Nr=64, B=1, ``L`` tokens, float32, with gate and skip."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("_ref_torch_ref", REF_TORCH)
+    tr = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tr)
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    B, H, N, P, Nr = 1, CFG2["H"], CFG2["N"], CFG2["P"], CFG2["Nr"]
+    g = torch.Generator().manual_seed(0)
+    f = torch.float32
+    # head-shared q / k and angles (as the layer produces them), expanded to the per-head
+    # layout the reference function takes
+    Q = (torch.randn(B, L, 1, N, generator=g, dtype=f) / math.sqrt(N)).expand(B, L, H, N).contiguous()
+    K = (torch.randn(B, L, 1, N, generator=g, dtype=f) / math.sqrt(N)).expand(B, L, H, N).contiguous()
+    V = torch.randn(B, L, H, P, generator=g, dtype=f)
+    Z = torch.randn(B, L, H, P, generator=g, dtype=f)
+    dt = torch.exp(torch.rand(B, H, L, generator=g, dtype=f) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+    adt = -(1.0 + 3.0 * torch.rand(H, generator=g, dtype=f))[None, :, None] * dt
+    trap = torch.randn(B, H, L, generator=g, dtype=f)
+    ang = (0.5 * torch.randn(B, L, 1, Nr, generator=g, dtype=f)).expand(B, L, H, Nr).contiguous()
+    qb = 0.1 * torch.randn(H, N, generator=g, dtype=f)
+    kb = 0.1 * torch.randn(H, N, generator=g, dtype=f)
+    dsk = torch.randn(H, generator=g, dtype=f)
+
+    def run():
+        with torch.no_grad():
+            tr.mamba3_siso_ref(Q, K, V, adt, dt, trap, qb, kb, ang, D=dsk, Z=Z)
+
+    run()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el > seconds:
+            break
+    return {"value": B * L * n / el, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"reference torch_ref.mamba3_siso_ref fp32 (baseline/_ref, unmodified), B=1 H=32 L={L} "
+                      f"N=128 P=64 Nr=64, gate and skip, {n} runs in {el:.1f}s"}
+
+
 # ----------------------------------------------------------------------------------------
 
 
 def run_reference(args, world, rank):
+    """The reference arm, on the host cores, each step a bounded sample of configs[1]'s forward.
+    Its value is the reference's chunked CPU algorithm (``reference.py``) through the oracle
+    restatement, since JAX is absent; beside it, the reference's own plain-torch code for the
+    path (``torch_ref.mamba3_siso_ref`` from the installed reference in baseline/_ref, the
+    recurrent form it pins parity with) is timed unmodified when the install is present."""
     if rank != 0:
         return 0
     cb = None
@@ -681,15 +738,18 @@ def run_reference(args, world, rank):
         cb = r
     v = statistics.median(vals)
     cb["value"] = v
+    tref = ref_torch_sample(seconds=8.0) if os.path.exists(REF_TORCH) else None
     line = {"metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 65536 / v * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "configs[1] kernel fwd B8 H32 L8192 N128 P64 chunk128 (CPU sample)",
                        "sample": cb["sample"]},
             "impl": "reference", "cpu_baseline": cb,
+            "torch_ref_baseline": tref,
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "JAX is absent here and on the GPU image, so reference.py / interpret-mode Pallas cannot run; "
-                    "the reference's CPU path is timed through its restatement in oracle/"}
+                    "the reference's chunked CPU path is timed through its restatement in oracle/, and the "
+                    "reference's own torch_ref.py (recurrent, plain torch) beside it as torch_ref_baseline"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -892,6 +952,8 @@ def main():
     # the CPU baseline first, on an idle host and before any GPU work, the way the reference
     # arm (a fresh process) takes it
     cpu = cpu_baseline_sample() if ("cpu" in what and rank == 0 and world == 1) else None
+    tref = (ref_torch_sample(seconds=5.0) if ("cpu" in what and rank == 0 and world == 1
+                                              and os.path.exists(REF_TORCH)) else None)
     # then the host side of every section on the CPUs local to this rank's GPU
     bind_to_gpu_cpus(torch.cuda.current_device())
     torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
@@ -965,6 +1027,8 @@ def main():
         line["seqpar_prefill"] = out["seqpar"]
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if tref is not None:
+        line["torch_ref_baseline"] = tref
     print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
