@@ -249,3 +249,52 @@ def test_decode_two_steps_in_a_row_at_scale():
         assert rel_error(y, y_ref) < TOL
     assert rel_error(sd.ssm, s_ref.ssm) < 1e-5
     assert rel_error(sd.k, s_ref.k) < 1e-5
+
+
+# ---- layer, configs[4] training shape --------------------------------------------------
+
+
+def test_layer_configs4_shape_bf16_forward_and_grads():
+    """The training benchmark's layer (d_model 512, d_state 128, headdim 64, H 16, chunk 128,
+    bf16 activations and matmul operands, fp32 parameters) through the package's autograd
+    node, forward and every parameter gradient, against float64 autograd through the oracle
+    layer (``layer.py:201-262``) on the same bf16-valued input and bf16-rounded projection
+    weights.  Bound: within 2e-2 normwise of exact, or no more than 1.5x as far from exact as
+    the reference kernels' own bf16 rounding scheme (the oracle with ``policy="bf16"``)."""
+    from mamba3_b200 import layer as LY
+    from tests.test_bwd_gpu import _normwise
+
+    cfg = LY.SISOConfig(d_model=512, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                        policy_name="bf16")
+    g = torch.Generator(device="cuda").manual_seed(41)
+    params = LY.init_params(cfg, key=4)
+    with torch.no_grad():  # non-trivial biases and gains, so their placement is exercised
+        for t in (params.b_bias, params.c_bias, params.b_norm_weight, params.c_norm_weight, params.d_skip):
+            t.add_(0.1 * torch.randn(t.shape, device="cuda", generator=g))
+        # the projections as the bf16 matmuls see them, so the oracle starts from the same weights
+        params.in_proj.copy_(params.in_proj.to(B16).float())
+        params.out_proj.copy_(params.out_proj.to(B16).float())
+    params = LY.SISOParams(*(t.detach().clone().requires_grad_(True) for t in params))
+    u = torch.randn(2, 1024, 512, device="cuda", generator=g).to(B16)
+    w = torch.randn(2, 1024, 512, device="cuda", generator=g)
+    y, st = LY.mamba3_siso_layer(params, u, cfg)
+    grads = torch.autograd.grad((y.float() * w).sum(), list(params))
+
+    def oracle(policy):
+        op = {k_: getattr(params, k_).detach().double().cpu().requires_grad_(True) for k_ in params._fields}
+        yr, sr = O.layer_forward(op, u.double().cpu(), d_state=128, headdim=64, nheads=cfg.nheads,
+                                 n_angles=cfg.n_angles, chunk=128, policy=policy)
+        gr = torch.autograd.grad((yr * w.double().cpu()).sum(), [op[k_] for k_ in params._fields])
+        return yr.detach(), sr, dict(zip(params._fields, gr))
+
+    y_ex, s_ex, g_ex = oracle("f32")
+    y_sc, _, g_sc = oracle("bf16")
+    rows = {"y": (_normwise(y, y_ex), _normwise(y_sc, y_ex)),
+            "ssm": (_normwise(st.ssm, s_ex.ssm), None)}
+    for i, k_ in enumerate(params._fields):
+        rows["d" + k_] = (_normwise(grads[i], g_ex[k_]), _normwise(g_sc[k_], g_ex[k_]))
+    print("\n[layer configs[4] shape] normwise vs exact: kernel | reference bf16 scheme")
+    for k_, (e, r) in rows.items():
+        print(f"    {k_:<16s} {e:.3e} | {'-' if r is None else f'{r:.3e}'}")
+    bad = {k_: (e, r) for k_, (e, r) in rows.items() if not e < max(TOL, 1.5 * (r or 0.0))}
+    assert not bad, f"further from exact than allowed (kernel, reference scheme): {bad}"
