@@ -8,7 +8,10 @@ gradients, ``tests.py:734-877`` decode).
   (B·H = 889 = 3·148·2 + 1) that leaves the last CTA with an odd tail;
 * the tensor-core forward and backward at H = 32, L = 8192, N = 128, P = 64, chunk 128
   (64 chunks of TMEM-carried state, 32-head dq / dk sums) on a sub-batch, with the
-  kernel-level benchmark's operand distributions.
+  kernel-level benchmark's operand distributions;
+* the layer at the training benchmark's shape (forward and parameter gradients, float64
+  oracle autograd) and a two-layer LM at the decode benchmark's layer shape (prefill then
+  128 decode steps against one forward).
 
 Each is checked against the float64 oracle.  The bf16 gradients use the normwise bound of
 the other bf16 gradient tests; the reference's p95 elementwise metric is printed beside it
@@ -298,3 +301,34 @@ def test_layer_configs4_shape_bf16_forward_and_grads():
         print(f"    {k_:<16s} {e:.3e} | {'-' if r is None else f'{r:.3e}'}")
     bad = {k_: (e, r) for k_, (e, r) in rows.items() if not e < max(TOL, 1.5 * (r or 0.0))}
     assert not bad, f"further from exact than allowed (kernel, reference scheme): {bad}"
+
+
+# ---- LM decode handoff, configs[3] layer shape -----------------------------------------
+
+
+@pytest.mark.parametrize("batch", [4, 16])
+def test_lm_prefill_then_decode_configs3_layer_shape(batch):
+    """The decode benchmark's layer (d_model 2048, H 64, N 128, P 64, Nr 32, gated MLP 4096,
+    bf16 weights), two layers: a 512-token prefill (tensor-core forward, carry out) then 128
+    decode steps (the decode kernel with fused B / C norms; batch 4 takes the batch-1..8
+    projection kernel, batch 16 the library GEMMs) give the logits of one 640-token forward.
+    The two paths round differently (the prefill reads out a bf16 state, the decode step an
+    fp32 one), so the bound is the bf16 one, normwise per step."""
+    from mamba3_b200 import layer as LY
+    from mamba3_b200 import model as M
+    from tests.test_bwd_gpu import _normwise
+
+    scfg = LY.SISOConfig(d_model=2048, d_state=128, headdim=64, expand=2, rope_fraction=0.5, chunk=128,
+                         policy_name="bf16")
+    cfg = M.LMConfig(vocab_size=512, n_layers=2, siso=scfg, d_intermediate=4096)
+    params = M.init_lm(cfg, key=3, dtype=torch.bfloat16)
+    toks = torch.randint(0, 512, (batch, 640), device="cuda", generator=torch.Generator(device="cuda").manual_seed(5))
+    with torch.no_grad():
+        full = M.lm_forward(params, toks, cfg).float()
+        _, st = M.lm_forward(params, toks[:, :512], cfg, states=M.zero_states(cfg, batch), logits="none")
+        errs = []
+        for t in range(512, 640):
+            lg, st = M.lm_decode_step(params, toks[:, t], st, cfg)
+            errs.append(_normwise(lg.float(), full[:, t]))
+    print(f"\n[lm configs[3] layer shape, batch {batch}] decode vs prefill logits, normwise per step: max {max(errs):.3e}, last {errs[-1]:.3e}")
+    assert max(errs) < TOL, errs
