@@ -50,6 +50,10 @@ def _rand(*shape, scale=1.0, seed=0):
     (100, 4096, 2048, True),    # ragged rows (one 128-row half only)
     (129, 512, 136, False),     # just over one half; an 8-column tail tile
     (1, 1024, 64, True),        # one row, a column tile of 64
+    (32, 2048, 8672, False),    # decode batch 32 per GPU
+    (30, 4096, 2048, True),     # rows not a multiple of 8
+    (64, 2048, 8192, False),
+    (120, 4096, 2048, True),
 ])
 def test_gemm_matches_fp32_product(m, k, n, res):
     from mamba3_b200 import projection as PJ
