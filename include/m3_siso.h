@@ -113,6 +113,10 @@ typedef struct M3FwdArgs {
    * there once instead of computing them once per head.  NULL is allowed (slower). */
   void *fwd_workspace;
   size_t fwd_workspace_bytes;
+  /* 1: fwd_workspace already holds the rates of these angles (an earlier call on the same
+   * angles and dims filled it, e.g. the states-only pass before the full one), so they are
+   * not computed again.  0: computed by this call. */
+  int32_t fwd_workspace_ready;
 } M3FwdArgs;
 
 /* Kernel selection for m3_siso_fwd / m3_siso_bwd.  AUTO uses the tcgen05 tensor-core kernel where it

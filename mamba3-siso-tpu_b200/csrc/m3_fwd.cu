@@ -155,11 +155,13 @@ static int run_fwd_ws(const M3FwdArgs& a, cudaStream_t s, uint8_t* tiles, float*
   const int nsm = sm_count();
   if (pre) {
     float* T = (float*)a.fwd_workspace;
-    const size_t n4 = (size_t)d.batch * d.seqlen * (d.n_angles / 4);
-    const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)nsm * 8);
-    ws::angle_rate_kernel<<<blocks, 256, 0, s>>>(a.angles, a.ang_st, d.batch, d.seqlen, d.n_angles, T);
-    int rc = check_launch("m3_siso_fwd (angle rates)");
-    if (rc != M3_OK) return rc;
+    if (!a.fwd_workspace_ready) {
+      const size_t n4 = (size_t)d.batch * d.seqlen * (d.n_angles / 4);
+      const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)nsm * 8);
+      ws::angle_rate_kernel<<<blocks, 256, 0, s>>>(a.angles, a.ang_st, d.batch, d.seqlen, d.n_angles, T);
+      int rc = check_launch("m3_siso_fwd (angle rates)");
+      if (rc != M3_OK) return rc;
+    }
     ex.T = T;
   }
   decltype(&ws::fwd_ws_kernel<true, false>) kerns[4] = {ws::fwd_ws_kernel<false, false>, ws::fwd_ws_kernel<true, false>,

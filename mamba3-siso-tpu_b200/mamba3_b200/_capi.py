@@ -54,6 +54,7 @@ class M3FwdArgs(ctypes.Structure):
         ("ybar", _vp), ("chunk_states", _vp), ("chunk_states_dtype", _i32),
         ("kernel", _i32), ("bwd_states", _vp), ("bwd_states_bytes", ctypes.c_size_t),
         ("fwd_workspace", _vp), ("fwd_workspace_bytes", ctypes.c_size_t),
+        ("fwd_workspace_ready", ctypes.c_int32),
     ]
 
 

@@ -121,7 +121,7 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
                      a_floor: float = 1e-4, chunk: int = 128, dtype_policy: str = "bf16",
                      y_out: Optional[torch.Tensor] = None, kernel: str = "auto",
                      bwd_states: Optional[torch.Tensor] = None, return_saved: bool = False,
-                     states_only: bool = False, lsplit: Optional[int] = None):
+                     states_only: bool = False, lsplit: Optional[int] = None, rates=None):
     """Fused boundary: raw ``(B, L, H)`` dt/A/trap streams and head-shared ``(B, L, Nr)``
     angles (all may be strided views of an in_proj output).  Returns
     ``(y, final_ssm, final_k, final_v, final_phi)``.  ``y_out`` may be a strided
@@ -135,7 +135,11 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
 
     ``lsplit``: cut every sequence into that many segments scanned side by side (see
     `_forward_raw_split`); ``None`` picks it from the SM count when the batch has too few
-    (b, h) sequences to fill the GPU, 1 never splits."""
+    (b, h) sequences to fill the GPU, 1 never splits.
+
+    ``rates``: ``(workspace, ready)`` -- a uint8 tensor of ``m3_siso_fwd_workspace_size``
+    bytes for the head-shared rotary rates, and whether an earlier call on the same angles
+    already filled it (the length split's two passes share one)."""
     if lsplit is None and not states_only and bwd_states is None and not return_saved:
         lsplit = _auto_split(q, v, angles, chunk, dtype_policy, kernel)
     if lsplit is not None and lsplit > 1 and not states_only and bwd_states is None and not return_saved:
@@ -187,8 +191,10 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     a.kernel = _kernel_code(kernel)
     # head-shared rotary rates, computed once per (b, t, angle) by the tensor-core forward
     wsz = C.lib().m3_siso_fwd_workspace_size(ctypes.byref(a.dims))
-    fws = torch.empty(wsz, dtype=torch.uint8, device=dev)
-    a.fwd_workspace, a.fwd_workspace_bytes = T.ptr(fws), wsz
+    fws, ready = rates if rates is not None else (None, False)
+    if fws is None or fws.numel() < wsz:
+        fws, ready = torch.empty(wsz, dtype=torch.uint8, device=dev), False
+    a.fwd_workspace, a.fwd_workspace_bytes, a.fwd_workspace_ready = T.ptr(fws), wsz, int(bool(ready))
     saved = False
     if bwd_states is not None and C.lib().m3_siso_fwd_saves_states(a):
         a.bwd_states, a.bwd_states_bytes = T.ptr(bwd_states), bwd_states.numel() * bwd_states.element_size()
@@ -234,12 +240,12 @@ def _auto_split(q, v, angles, chunk, dtype_policy, kernel) -> int:
 
 def forward_launches(q, v, angles, chunk, dtype_policy="bf16", kernel="auto", lsplit=None) -> int:
     """Kernel launches of one `siso_forward_raw` call with these shapes (no saved states):
-    2 for the tensor-core forward (head-shared rotary rates + the scan), 7 when it is split
-    over the length (tile sums, entering angles, the states-only and the full pass with
-    their rate passes, the carry rebuild), 1 for the generic kernel."""
+    2 for the tensor-core forward (head-shared rotary rates + the scan), 6 when it is split
+    over the length (tile sums, entering angles, one rate pass shared by the states-only and
+    the full pass, the carry rebuild), 1 for the generic kernel."""
     g = _auto_split(q, v, angles, chunk, dtype_policy, kernel) if lsplit is None else lsplit
     if g > 1:
-        return 7
+        return 6
     tc = kernel in ("auto", "tensorcore", "tensorcore_v1") and final_state_supported(q, v, angles, chunk,
                                                                                        dtype_policy)
     return 2 if tc else 1
@@ -315,8 +321,12 @@ def _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias
     ca = C.M3SplitCarryArgs(b, h, g, tiles, n, p, nr, T.ptr(partial), T.ptr(a_seg), T.ptr(coef), None, None, None,
                             *(T.ptr(t) for t in seeds), T.ptr(phi_in), None, None, None)
     C.check(C.lib().m3_siso_split_carry(ctypes.byref(ca), stream))
+    # both passes read the same head-shared rotary rates: computed by the first, reused by the second
+    d_seg = C.M3Dims(b * g, l // g, h, n, p, nr, chunk)
+    rws = torch.empty(C.lib().m3_siso_fwd_workspace_size(ctypes.byref(d_seg)), dtype=torch.uint8, device=dev)
     _, s_loc, k_last, v_last, _ = siso_forward_raw(qs, ks, vs, *raws, dt_bias, q_bias, k_bias, z=zs,
-                                                   seed_phi=phi_in, states_only=True, **common)
+                                                   seed_phi=phi_in, states_only=True, rates=(rws, False),
+                                                   **common)
     c_ssm = torch.empty(b * g, h, p, n, dtype=f32, device=dev)
     c_k = torch.empty(b * g, h, n, dtype=f32, device=dev)
     c_v = torch.empty(b * g, h, p, dtype=f32, device=dev)
@@ -332,7 +342,8 @@ def _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias
         y_out = torch.empty(b, l, h, p, dtype=io, device=dev).permute(0, 2, 1, 3)
     ys = _split_view_bhlp(y_out, g)
     _, fs, fk, fv, fphi = siso_forward_raw(qs, ks, vs, *raws, dt_bias, q_bias, k_bias, z=zs, seed_ssm=c_ssm,
-                                           seed_k=c_k, seed_v=c_v, seed_phi=phi_in, y_out=ys, **common)
+                                           seed_k=c_k, seed_v=c_v, seed_phi=phi_in, y_out=ys, rates=(rws, True),
+                                           **common)
     if target is not None and target.data_ptr() != y_out.data_ptr():
         target.copy_(y_out)
         y_out = target

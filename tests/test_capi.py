@@ -38,8 +38,8 @@ def test_struct_layout_matches_header():
 int main(void) {
   printf("%zu %zu %zu %zu %zu\n", sizeof(M3Dims), sizeof(M3Strides), sizeof(M3FwdArgs),
          sizeof(M3BwdArgs), sizeof(M3DecodeArgs));
-  printf("%zu %zu %zu\n", offsetof(M3FwdArgs, chunk_states_dtype), offsetof(M3BwdArgs, workspace_bytes),
-         offsetof(M3DecodeArgs, y));
+  printf("%zu %zu %zu %zu\n", offsetof(M3FwdArgs, chunk_states_dtype), offsetof(M3BwdArgs, workspace_bytes),
+         offsetof(M3DecodeArgs, y), offsetof(M3FwdArgs, fwd_workspace_ready));
   printf("%zu %zu %zu %zu\n", sizeof(M3SampleArgs), offsetof(M3SampleArgs, seed), offsetof(M3SampleArgs, stop_ids),
          offsetof(M3SampleArgs, probs_ld));
   printf("%zu %zu %zu %zu\n", sizeof(M3SplitPrepArgs), offsetof(M3SplitPrepArgs, coef), sizeof(M3SplitCarryArgs),
@@ -59,6 +59,7 @@ int main(void) {
     want = [ctypes.sizeof(C.M3Dims), ctypes.sizeof(C.M3Strides), ctypes.sizeof(C.M3FwdArgs),
             ctypes.sizeof(C.M3BwdArgs), ctypes.sizeof(C.M3DecodeArgs),
             C.M3FwdArgs.chunk_states_dtype.offset, C.M3BwdArgs.workspace_bytes.offset, C.M3DecodeArgs.y.offset,
+            C.M3FwdArgs.fwd_workspace_ready.offset,
             ctypes.sizeof(C.M3SampleArgs), C.M3SampleArgs.seed.offset, C.M3SampleArgs.stop_ids.offset,
             C.M3SampleArgs.probs_ld.offset,
             ctypes.sizeof(C.M3SplitPrepArgs), C.M3SplitPrepArgs.coef.offset, ctypes.sizeof(C.M3SplitCarryArgs),
