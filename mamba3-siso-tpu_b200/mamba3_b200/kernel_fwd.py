@@ -142,6 +142,10 @@ def siso_forward_raw(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, 
     already filled it (the length split's two passes share one)."""
     if lsplit is None and not states_only and bwd_states is None and not return_saved:
         lsplit = _auto_split(q, v, angles, chunk, dtype_policy, kernel)
+        if lsplit == 1 and _chain_fits(q, v, angles, chunk, dtype_policy, kernel):
+            return _forward_raw_chain2(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z,
+                                       seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, dtype_policy, y_out,
+                                       kernel)
     if lsplit is not None and lsplit > 1 and not states_only and bwd_states is None and not return_saved:
         return _forward_raw_split(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z,
                                   seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, dtype_policy, y_out, kernel,
@@ -238,6 +242,65 @@ def _auto_split(q, v, angles, chunk, dtype_policy, kernel) -> int:
     return best if best >= _MIN_SEGMENTS else 1
 
 
+_ST_COST = 0.68  # states-only pass per chunk, relative to the full forward (measured)
+_MIN_CHAIN_CHUNKS = 16
+
+
+def _chain_fits(q, v, angles, chunk, dtype_policy, kernel) -> bool:
+    """Whether `_forward_raw_chain2` applies: the (b, h) sequences fill at most half the SMs
+    (so two passes run side by side) but too many for the length split's equal segments."""
+    if kernel not in ("auto", "tensorcore") or not final_state_supported(q, v, angles, chunk, dtype_policy):
+        return False
+    units = q.shape[0] * v.shape[1]
+    return 2 * units <= _sm_count(q.device) and q.shape[1] // chunk >= _MIN_CHAIN_CHUNKS
+
+
+def _chain_cut(nck: int) -> int:
+    """Chunks of the first segment: the full pass of segment 0 (a chunks) ends when the
+    states-only pass of segment 0 plus the full pass of segment 1 do, a = _ST_COST a + (nck - a)."""
+    return min(nck - 1, max(1, round(nck / (2.0 - _ST_COST))))
+
+
+_SIDE_STREAMS = {}
+
+
+def _forward_raw_chain2(q, k, v, dt_raw, a_raw, trap_raw, angles, dt_bias, q_bias, k_bias, d_skip, z,
+                        seed_ssm, seed_k, seed_v, seed_phi, a_floor, chunk, dtype_policy, y_out, kernel):
+    """The forward of a batch that fills at most half the SMs, as two chained segments of
+    unequal length whose passes overlap: on a side stream the full forward of segment 0
+    (tokens [0, a)); on the caller's stream the states-only pass of segment 0 (its exact
+    final carry, from the caller's carry), then the full forward of segment 1 from that carry
+    (the segment chaining of ``siso.py:154-216``).  Both streams hold B * H persistent CTAs,
+    so they run side by side; ``a`` balances segment 0's full pass against the states-only
+    pass plus segment 1 (`_chain_cut`).  Same results as one pass of the whole sequence."""
+    b, l, _ = q.shape
+    h, p = v.shape[1], v.shape[3]
+    cut = _chain_cut(l // chunk) * chunk
+    dev = q.device
+    io = v.dtype if v.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    if y_out is None:
+        y_out = torch.empty(b, h, l, p, dtype=io, device=dev)
+    common = dict(d_skip=d_skip, a_floor=a_floor, chunk=chunk, dtype_policy=dtype_policy, kernel=kernel, lsplit=1)
+    sl0, sl1 = slice(0, cut), slice(cut, l)
+    seg = lambda sl: (q[:, sl], k[:, sl], v[:, :, sl], dt_raw[:, sl], a_raw[:, sl], trap_raw[:, sl], angles[:, sl])
+    z0 = None if z is None else z[:, :, sl0]
+    z1 = None if z is None else z[:, :, sl1]
+    seeds = dict(seed_ssm=seed_ssm, seed_k=seed_k, seed_v=seed_v, seed_phi=seed_phi)
+    cur = torch.cuda.current_stream(dev)
+    side = _SIDE_STREAMS.get(dev)
+    if side is None:
+        side = _SIDE_STREAMS[dev] = torch.cuda.Stream(dev)
+    side.wait_stream(cur)
+    with torch.cuda.stream(side):
+        siso_forward_raw(*seg(sl0), dt_bias, q_bias, k_bias, z=z0, y_out=y_out[:, :, sl0], **seeds, **common)
+    _, s0, k0, v0, p0 = siso_forward_raw(*seg(sl0), dt_bias, q_bias, k_bias, z=z0, states_only=True, **seeds,
+                                         **common)
+    _, fs, fk, fv, fphi = siso_forward_raw(*seg(sl1), dt_bias, q_bias, k_bias, z=z1, y_out=y_out[:, :, sl1],
+                                           seed_ssm=s0, seed_k=k0, seed_v=v0, seed_phi=p0, **common)
+    cur.wait_stream(side)
+    return y_out, fs, fk, fv, fphi
+
+
 def forward_launches(q, v, angles, chunk, dtype_policy="bf16", kernel="auto", lsplit=None) -> int:
     """Kernel launches of one `siso_forward_raw` call with these shapes (no saved states):
     2 for the tensor-core forward (head-shared rotary rates + the scan), 6 when it is split
@@ -246,6 +309,8 @@ def forward_launches(q, v, angles, chunk, dtype_policy="bf16", kernel="auto", ls
     g = _auto_split(q, v, angles, chunk, dtype_policy, kernel) if lsplit is None else lsplit
     if g > 1:
         return 6
+    if lsplit is None and _chain_fits(q, v, angles, chunk, dtype_policy, kernel):
+        return 6  # rates + pass for each of the three calls
     tc = kernel in ("auto", "tensorcore", "tensorcore_v1") and final_state_supported(q, v, angles, chunk,
                                                                                        dtype_policy)
     return 2 if tc else 1
