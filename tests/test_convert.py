@@ -174,10 +174,10 @@ def test_checkpoint_rejects_bad_files(tmp_path):
     with np.load(path) as z:
         arrays = {k: z[k] for k in z.files}
     np.savez(tmp_path / "missing.npz", **{k: v for k, v in arrays.items() if k != "final_norm"})
-    with pytest.raises(ValueError, match="missing"):
+    with pytest.raises(ValueError, match="'final_norm' not found"):
         CP.load(str(tmp_path / "missing.npz"))
     np.savez(tmp_path / "extra.npz", stray=np.zeros(3), **arrays)
-    with pytest.raises(ValueError, match="unexpected"):
+    with pytest.raises(ValueError, match="does not account for"):
         CP.load(str(tmp_path / "extra.npz"))
     bad = dict(arrays)
     bad["embed"] = bad["embed"][:, :5]
