@@ -848,19 +848,27 @@ def run_profile_case(which):
         if not hasattr(lib, "m3_debug_ws_timing"):
             raise SystemExit("fwdphases: rebuild with build.build(force=True, extra=['-DM3_WS_TIMING'])")
         lib.m3_debug_ws_timing.argtypes = [ctypes.POINTER(ctypes.c_ulonglong), ctypes.c_int]
+        from mamba3_b200 import kernel_fwd as KF
         c = dict(CFG2)
         d = make_cfg2_inputs(c, 0)
-        for _ in range(3):
-            fwd_call(d, c)
-        torch.cuda.synchronize()
-        buf = (ctypes.c_ulonglong * 256)()
-        lib.m3_debug_ws_timing(buf, 1)
-        fwd_call(d, c)
-        torch.cuda.synchronize()
-        lib.m3_debug_ws_timing(buf, 1)
-        for code in range(128):  # per code: cycles per call (a wait site or a phase of one role)
-            if buf[128 + code]:
-                print(f"code {code:3d}: {buf[code] / buf[128 + code]:9.1f} cycles over {buf[128 + code]} calls")
+        v, z = d["x"].permute(0, 2, 1, 3), d["z"].permute(0, 2, 1, 3)
+        for so in (False, True):  # the full forward, then its states-only mode
+            def call():
+                return KF.siso_forward_raw(d["q"], d["k"], v, d["dt_raw"], d["a_raw"], d["trap_raw"], d["angles"],
+                                           d["dt_bias"], d["q_bias"], d["k_bias"], d_skip=d["d_skip"], z=z,
+                                           chunk=c["chunk"], dtype_policy="bf16", lsplit=1, states_only=so)
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+            buf = (ctypes.c_ulonglong * 256)()
+            lib.m3_debug_ws_timing(buf, 1)
+            call()
+            torch.cuda.synchronize()
+            lib.m3_debug_ws_timing(buf, 1)
+            print("states-only" if so else "full")
+            for code in range(128):  # per code: cycles per call (a wait site or a phase of one role)
+                if buf[128 + code]:
+                    print(f"code {code:3d}: {buf[code] / buf[128 + code]:9.1f} cycles over {buf[128 + code]} calls")
         return 0
     if which == "bwdphases":  # needs a library built with -DM3_TC_TIMING (diagnostic)
         import ctypes
