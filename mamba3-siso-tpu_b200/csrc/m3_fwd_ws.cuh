@@ -20,7 +20,11 @@
 //   warps 12-15 state and output (thread = TMEM lane): the state pass (bf16 state tile for
 //               the next readout, scaling by the next chunk's exp2(A_last), final state),
 //               the decay mask S -> P (bf16, into TMEM over the S columns just read), the
-//               accumulator seed exp2(A) Yi + (D + gamma u.w) v, the gated output.
+//               accumulator seed exp2(A) Yi + (D + gamma u.w) v, the gated output.  In the
+//               states-only mode, which has no output, they instead rotate half of each
+//               chunk's k rows two chunks ahead (the rotary warps pass the angles through
+//               the unused q tile), so the rotary warps, the critical role, do half the
+//               rotation.
 //
 // TMEM (512 columns): S[2] 0..255, Yi[2] 256..383, the fp32 state 384..447 (lane n,
 // column p), the output accumulator 448..511; the bf16 mask P of a chunk is written over
@@ -68,6 +72,7 @@ struct Small {
   // (eight groups) reads 128 contiguous bytes.
   float bias[2][4][2][8][4];
   uint64_t full_qk[2], full_v[2], rot_done[2], mma1[2], mma2[2], p_ready[2], yfree[2], zfull[2], ystaged[2];
+  uint64_t ang_ready[2];  // states-only mode: angles of the tokens the state warps rotate
   uint64_t scal_ready[3], scal_free[3];
   uint64_t state_ready, drain;
   uint32_t tmem;
@@ -309,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       umma::mbar_init(&sm->full_qk[s], 1);
       umma::mbar_init(&sm->full_v[s], 1);
-      umma::mbar_init(&sm->rot_done[s], 8);
+      umma::mbar_init(&sm->rot_done[s], ST ? 12 : 8);  // states-only: the state warps rotate too
+      umma::mbar_init(&sm->ang_ready[s], 8);
       umma::mbar_init(&sm->mma1[s], 1);
       umma::mbar_init(&sm->mma2[s], 1);
       umma::mbar_init(&sm->p_ready[s], 4);
@@ -683,8 +689,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sQ = st + kOQ;
         uint8_t* sK = st + kOK;
         float sclr = sclj[0];
+        // states-only mode: the state warps, idle but for the state pass, rotate the last two
+        // tokens of every quad; their absolute angles (turns) go through the q tile, which
+        // this mode does not load
+        constexpr int kRotTok = ST ? 2 : 4;
 #pragma unroll 1
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < kRotTok; ++j) {
           const int t = tl + j;
           // sin / cos of the angle reduced to [-pi, pi] (the SFU's accurate range)
           float cs[8], sn[8];
@@ -760,6 +770,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           sclr = j == 0 ? sclj[1] : j == 1 ? sclj[2] : sclj[3];
         }
+        if constexpr (ST) {  // ph[0], ph[1] now hold tokens tl + 2, tl + 3
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            float* dst = reinterpret_cast<float*>(sQ + (tl + 2 + j) * 256 + 32 * g);
+            *reinterpret_cast<float4*>(dst) = make_float4(ph[j][0], ph[j][1], ph[j][2], ph[j][3]);
+            *reinterpret_cast<float4*>(dst + 4) = make_float4(ph[j][4], ph[j][5], ph[j][6], ph[j][7]);
+          }
+          __syncwarp();
+          if (lane == 0) arrive(&sm->ang_ready[s]);
+        }
         WS_MARK(86);
         // ---- vd = v exp2(A_last - A) for this warp's 16 rows --------------------------
         if (!ST && G >= 2) yok = yok && wait_warp(sm, &sm->yfree[s], ((G - 2) >> 1) & 1, 63);
@@ -795,6 +815,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lrow = (uint32_t)(32 * qd) << 16;
     uint32_t G = 0;
     bool ok = true;
+    // states-only mode: rotate tokens 4m + 2, 4m + 3 of chunk cr (pipeline index Gr) into the
+    // khat tile, from the angles the rotary warps left in the q tile; then count towards
+    // rot_done.  Item = (one of those 64 tokens, an 8-angle group); four per thread.
+    auto st_rotate = [&](uint32_t Gr, int cr, int u_, size_t bh_) -> bool {
+      const int sr = Gr & 1, s3r = Gr % 3;
+      uint8_t* str = base + sr * kStageBytes;
+      if (!wait_warp(sm, &sm->ang_ready[sr], (Gr >> 1) & 1, 76)) return false;
+      if (!wait_warp(sm, &sm->full_qk[sr], (Gr >> 1) & 1, 77)) return false;
+      uint8_t* sK = str + kOK;
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int idx = i + 128 * m, tok = idx >> 3, g = idx & 7;
+        const int t = 4 * (tok >> 1) + 2 + (tok & 1);
+        const bool grot = 8 * g < Nr;
+        const float* ap = reinterpret_cast<const float*>(str + kOQ + t * 256 + 32 * g);
+        const float4 a0 = *reinterpret_cast<const float4*>(ap), a1 = *reinterpret_cast<const float4*>(ap + 4);
+        const float ang[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        float cs[8], sn[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (grot) {
+            const float xs = frac_centered(ang[e]) * kTwoPi;
+            cs[e] = cos_approx(xs);
+            sn[e] = sin_approx(xs);
+          } else {
+            cs[e] = 1.f;
+            sn[e] = 0.f;
+          }
+        }
+        const uint32_t soff = umma::sw128_off(t, g);
+        const uint4 ukl = *reinterpret_cast<const uint4*>(sK + soff);
+        const uint4 ukh = *reinterpret_cast<const uint4*>(sK + 16384 + soff);
+        const uint32_t kl[4] = {ukl.x, ukl.y, ukl.z, ukl.w}, kh[4] = {ukh.x, ukh.y, ukh.z, ukh.w};
+        const float2 sc2 = f2s(sm->scl[s3r][t]);
+        const bool fin = a.final_k && cr == nchunk - 1 && t == kC - 1;
+        uint32_t ok_lo[4], ok_hi[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 c2 = f2(cs[2 * e], cs[2 * e + 1]), s2 = f2(sn[2 * e], sn[2 * e + 1]);
+          const float4 bk = *reinterpret_cast<const float4*>(sm->bias[u_ & 1][e][1][g]);
+          const float2 wlo = add2(bf2f(kl[e]), f2(bk.x, bk.y));
+          const float2 whi = add2(bf2f(kh[e]), f2(bk.z, bk.w));
+          const float2 ns2 = f2(-s2.x, -s2.y);
+          const float2 klo = fma2(whi, ns2, mul2(wlo, c2));
+          const float2 khi = fma2(wlo, s2, mul2(whi, c2));
+          if (fin) {  // the final k is rotated but unscaled
+            float* fk = a.final_k + bh_ * kN + 8 * g + 2 * e;
+            fk[0] = klo.x;
+            fk[1] = klo.y;
+            fk[64] = khi.x;
+            fk[65] = khi.y;
+          }
+          ok_lo[e] = f2bf(mul2(klo, sc2));
+          ok_hi[e] = f2bf(mul2(khi, sc2));
+        }
+        *reinterpret_cast<uint4*>(sK + soff) = make_uint4(ok_lo[0], ok_lo[1], ok_lo[2], ok_lo[3]);
+        *reinterpret_cast<uint4*>(sK + 16384 + soff) = make_uint4(ok_hi[0], ok_hi[1], ok_hi[2], ok_hi[3]);
+      }
+      umma::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) arrive(&sm->rot_done[sr]);
+      return true;
+    };
     for (int u = blockIdx.x; u < ex.nunits && ok; u += gridDim.x) {
       const int b = u / H, h = u % H;
       const size_t bh = (size_t)u;
@@ -888,6 +971,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
+      if constexpr (ST) {  // two chunks ahead of the state update they feed
+        if (!(ok = st_rotate(G, 0, u, bh))) break;
+        if (nchunk > 1 && !(ok = st_rotate(G + 1, 1, u, bh))) break;
+      }
       for (int c = 0; c < nchunk; ++c, ++G) {
         const int s = G & 1;
         const bool last = c == nchunk - 1;
@@ -954,6 +1041,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       (size_t)(L - 1) * a.v_st.l;
             a.final_v[bh * kP + i] = __bfloat162float(vr[i]);
           }
+          if (c + 2 < nchunk && !(ok = st_rotate(G + 2, c + 2, u, bh))) break;
           continue;
         }
         // ---- output of the previous chunk ------------------------------------------------
